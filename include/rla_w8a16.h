@@ -1,0 +1,153 @@
+/*
+ * rla_w8a16.h -- C ABI of the B200 (sm_100a) W8A16 GEMM library.
+ *
+ * W8A16: fp16 activations x int8 weights with one symmetric scale per output
+ * channel, fp32 accumulation, fp16 output:
+ *
+ *     y[m, n] = fp16( scale[n] * sum_k x[m, k] * w[n, k]  (+ bias[n]) )
+ *
+ * Plain pointers and sizes only (no framework types).  Device pointers are
+ * CUDA device addresses on the current device; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).  Every entry point returns an rla_status;
+ * nothing throws across this boundary.  rla_last_error() gives a message for
+ * the last failure on the calling thread.
+ *
+ * Each entry point names the rotalabs-accel interface it replaces
+ * (paths inside the rotalabs-accel project).
+ */
+#ifndef RLA_W8A16_H
+#define RLA_W8A16_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RLA_API __attribute__((visibility("default")))
+#else
+#define RLA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum rla_status {
+  RLA_OK = 0,
+  RLA_ERR_INVALID_ARGUMENT = 1, /* bad size, stride, dtype or null pointer      */
+  RLA_ERR_UNSUPPORTED = 2,      /* valid request this build cannot run          */
+  RLA_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed         */
+  RLA_ERR_WORKSPACE = 4,        /* workspace missing, too small or misaligned   */
+  RLA_ERR_DEVICE = 5            /* no device, or not an sm_100 device           */
+} rla_status;
+
+typedef enum rla_dtype {
+  RLA_DTYPE_NONE = 0, /* "no tensor" (e.g. no bias) */
+  RLA_DTYPE_F16 = 1,
+  RLA_DTYPE_F32 = 2,
+  RLA_DTYPE_BF16 = 3
+} rla_dtype;
+
+/* Kernel families the per-shape selector can pick. */
+typedef enum rla_kernel {
+  RLA_KERNEL_NONE = 0,     /* nothing to compute (M == 0 or N == 0)              */
+  RLA_KERNEL_SKINNY = 1,   /* HBM-streaming split-K kernel, M <= 32 (decode)     */
+  RLA_KERNEL_TCGEN05 = 2,  /* TMA + int8->fp16 into TMEM + tcgen05.mma (prefill) */
+  RLA_KERNEL_GENERIC = 3,  /* any alignment / any K (ragged shapes)              */
+  RLA_KERNEL_FILL = 4      /* K == 0: y = bias (or 0)                            */
+} rla_kernel;
+
+/*
+ * W8A16 GEMM on device buffers.
+ *
+ * Replaces rotalabs-accel's GPU launch of the Triton kernel
+ * (src/rotalabs_accel/kernels/gemm.py:140-186, `_int8_gemm_triton` ->
+ * `_int8_gemm_kernel[grid](...)` at :169-178, with the separate bias add at
+ * :180-182) behind the dispatcher `int8_gemm` (gemm.py:189-238).
+ *
+ *   x      fp16 [M, K], row stride ldx elements (ldx >= K)
+ *   w      int8 [N, K], row stride ldw bytes    (ldw >= K), K contiguous
+ *          (the reference's `weight_int8` layout; no transposed copy is used)
+ *   scale  [N], scale_dtype RLA_DTYPE_F32 (Int8Linear) or RLA_DTYPE_F16
+ *   bias   [N] or NULL; bias_dtype RLA_DTYPE_NONE / F16 / F32
+ *   y      fp16 [M, N], row stride ldy elements (ldy >= N)
+ *   workspace / workspace_bytes: caller-owned device scratch for split-K
+ *          partial sums, at least rla_w8a16_workspace_size(M, N, K) bytes,
+ *          256-byte aligned.  Layout: the first 4096 bytes hold arrival
+ *          counters that must be zero before the first call (the library
+ *          leaves them at zero after every call, so one workspace serves
+ *          calls of any shape); fp32 partial sums follow.  May be NULL / 0:
+ *          the selector then plans without split-K.  Calls that share a
+ *          workspace must be stream-ordered.
+ *   stream cudaStream_t to launch on.
+ *
+ * Returns RLA_OK, or an error with nothing launched.
+ */
+RLA_API int rla_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
+                   int scale_dtype, const void* bias, int bias_dtype, void* y, int64_t ldy, int64_t M,
+                   int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace the selector's plan for (M, N, K) can use (0 if none).
+ * Part of the same replacement as rla_w8a16_gemm (gemm.py:140-186). */
+RLA_API size_t rla_w8a16_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/*
+ * The per-shape kernel selector (replaces the Triton autotuner keyed on
+ * (M, N, K), src/rotalabs_accel/kernels/gemm.py:53-65).  Describes the plan
+ * rla_w8a16_gemm would run for this call without launching anything:
+ * kernel family (rla_kernel) and its launch parameters.  `aligned` = 1 when
+ * x, w are 16-byte aligned, ldx % 8 == 0 and ldw % 16 == 0.  `params`
+ * (may be NULL) receives up to 8 integers: [0] kernel, [1] grid.x,
+ * [2] grid.y, [3] threads per CTA, [4] split-K slices, [5] tile rows of w,
+ * [6] tile rows of x, [7] dynamic shared memory bytes.
+ */
+RLA_API int rla_w8a16_plan(int64_t M, int64_t N, int64_t K, int aligned, int have_workspace, int64_t* params);
+
+/*
+ * Per-output-channel symmetric int8 quantization on the device.
+ *
+ * Replaces quantize_weight_per_channel
+ * (src/rotalabs_accel/quantization/symmetric.py:126-151 ->
+ * quantize_symmetric(dim=1), :24-82), bit-identical to it: per row,
+ * scale = max|w| / 127 computed in the input dtype, 0 -> 1, then
+ * q = round_half_even(w / scale) (quotient rounded to the input dtype first,
+ * as torch does) clamped to [-128, 127]; scale is returned as fp32.
+ *
+ *   w      [N, K] of w_dtype (F32, F16 or BF16), row stride ldw elements
+ *   q      int8 [N, K], row stride ldq bytes
+ *   scale  fp32 [N]
+ */
+RLA_API int rla_quantize_per_channel(const void* w, int w_dtype, int64_t ldw, int64_t N, int64_t K, int8_t* q,
+                             int64_t ldq, float* scale, void* stream);
+
+/*
+ * Column-parallel assembly: the all-gathered staging buffer
+ * staging[world][M][n_local] (fp16, contiguous; what ncclAllGather of each
+ * rank's [M, n_local] output slice produces) is rearranged into
+ * y[M][world * n_local] (row stride ldy).  No counterpart in rotalabs-accel,
+ * which has no distributed code; it is the output step of the column-parallel
+ * sharded Int8Linear (each rank holds rows [r*n_local, (r+1)*n_local) of
+ * weight_int8 / scale, src/rotalabs_accel/kernels/gemm.py:268-279).
+ */
+RLA_API int rla_gather_columns(const void* staging, int64_t world, int64_t M, int64_t n_local, void* y, int64_t ldy,
+                       void* stream);
+
+/* Number of kernels this library has launched in this process (all devices). */
+RLA_API uint64_t rla_launch_count(void);
+
+/* Reads and clears the device-side error word of the current device (0 = no
+ * error; otherwise a bounded wait inside a kernel gave up: 1 TMA tile,
+ * 2 free slot, 3 converted operand, 4 operand slot, 5 accumulator,
+ * 6 split-K partner).  Synchronises the device. */
+RLA_API int rla_get_device_error(unsigned int* code);
+
+/* Message for the last non-OK status returned on this thread ("" if none). */
+RLA_API const char* rla_last_error(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+RLA_API int rla_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RLA_W8A16_H */

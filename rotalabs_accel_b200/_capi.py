@@ -1,0 +1,189 @@
+"""ctypes binding of the C ABI in ``include/rla_w8a16.h``.
+
+The shared library ``librla_w8a16.so`` is built in-tree
+(``rotalabs_accel_b200/build.py``) and loaded from this package directory.
+Every CUDA computation of the package goes through here; if the library is
+missing or does not load, calls raise instead of computing anything another
+way.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "librla_w8a16.so")
+
+RLA_OK = 0
+DTYPE_NONE, DTYPE_F16, DTYPE_F32, DTYPE_BF16 = 0, 1, 2, 3
+KERNEL_NAMES = {0: "none", 1: "skinny", 2: "tcgen05", 3: "generic", 4: "fill"}
+
+EXPORTED_SYMBOLS = (
+    "rla_w8a16_gemm", "rla_w8a16_workspace_size", "rla_w8a16_plan", "rla_quantize_per_channel",
+    "rla_gather_columns", "rla_launch_count", "rla_get_device_error", "rla_last_error", "rla_version",
+)
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+class RlaError(RuntimeError):
+    """A C-ABI call returned a non-OK status."""
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load (once) and type the C ABI.  Raises if the library is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"rotalabs_accel_b200: CUDA library {path} is missing; build it with "
+                "`python -m rotalabs_accel_b200.build` (there is no non-CUDA path for CUDA tensors)")
+        lib = ctypes.CDLL(path)
+        i64, p, sz = ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t
+        lib.rla_w8a16_gemm.argtypes = [p, i64, p, i64, p, ctypes.c_int, p, ctypes.c_int, p, i64,
+                                       i64, i64, i64, p, sz, p]
+        lib.rla_w8a16_gemm.restype = ctypes.c_int
+        lib.rla_w8a16_workspace_size.argtypes = [i64, i64, i64]
+        lib.rla_w8a16_workspace_size.restype = sz
+        lib.rla_w8a16_plan.argtypes = [i64, i64, i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(i64)]
+        lib.rla_w8a16_plan.restype = ctypes.c_int
+        lib.rla_quantize_per_channel.argtypes = [p, ctypes.c_int, i64, i64, i64, p, i64, p, p]
+        lib.rla_quantize_per_channel.restype = ctypes.c_int
+        lib.rla_gather_columns.argtypes = [p, i64, i64, i64, p, i64, p]
+        lib.rla_gather_columns.restype = ctypes.c_int
+        lib.rla_launch_count.argtypes = []
+        lib.rla_launch_count.restype = ctypes.c_uint64
+        lib.rla_get_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint)]
+        lib.rla_get_device_error.restype = ctypes.c_int
+        lib.rla_last_error.argtypes = []
+        lib.rla_last_error.restype = ctypes.c_char_p
+        lib.rla_version.argtypes = []
+        lib.rla_version.restype = ctypes.c_int
+        _lib = lib
+        return lib
+
+
+def _check(status: int, what: str) -> None:
+    if status != RLA_OK:
+        msg = load_library().rla_last_error().decode(errors="replace")
+        raise RlaError(f"{what} failed with status {status}: {msg}")
+
+
+def _scale_dtype(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return DTYPE_F32
+    if t.dtype == torch.float16:
+        return DTYPE_F16
+    raise TypeError(f"scale must be float32 or float16, got {t.dtype}")
+
+
+def _bias_dtype(t) -> int:
+    if t is None:
+        return DTYPE_NONE
+    if t.dtype == torch.float16:
+        return DTYPE_F16
+    if t.dtype == torch.float32:
+        return DTYPE_F32
+    raise TypeError(f"bias must be float16 or float32, got {t.dtype}")
+
+
+# Split-K workspaces: one per (device, stream), zero-filled on allocation and
+# grown on demand.  Calls on one stream are ordered, so sharing is safe.
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, stream_ptr: int, nbytes: int) -> torch.Tensor:
+    key = (device.index, stream_ptr)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def plan(M: int, N: int, K: int, aligned: bool = True, have_workspace: bool = True) -> dict:
+    """The selector's plan for a shape (no launch)."""
+    lib = load_library()
+    params = (ctypes.c_int64 * 8)()
+    _check(lib.rla_w8a16_plan(M, N, K, int(aligned), int(have_workspace), params), "rla_w8a16_plan")
+    keys = ("kernel", "grid_x", "grid_y", "threads", "splits", "w_rows", "x_rows", "smem")
+    d = dict(zip(keys, list(params)))
+    d["kernel_name"] = KERNEL_NAMES.get(d["kernel"], "?")
+    return d
+
+
+def w8a16_gemm(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor, bias=None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """``y[M, N] = fp16(x2d @ (weight_int8 * scale[:, None]).T + bias)`` on
+    the current CUDA stream through ``rla_w8a16_gemm``.
+
+    ``x2d`` fp16 ``[M, K]`` with unit inner stride; ``weight_int8`` int8
+    ``[N, K]`` with unit inner stride; ``scale`` ``[N]`` fp32/fp16
+    contiguous; ``bias`` ``[N]`` fp16/fp32 or None."""
+    lib = load_library()
+    M, K = x2d.shape
+    N = weight_int8.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=x2d.device)
+    stream = torch.cuda.current_stream(x2d.device).cuda_stream
+    need = lib.rla_w8a16_workspace_size(M, N, K)
+    ws_ptr, ws_bytes = None, 0
+    if need:
+        ws = _workspace(x2d.device, stream, need)
+        ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(x2d.device):
+        st = lib.rla_w8a16_gemm(
+            x2d.data_ptr(), x2d.stride(0) if M > 0 else K, weight_int8.data_ptr(),
+            weight_int8.stride(0) if N > 0 else K, scale.data_ptr(), _scale_dtype(scale),
+            bias.data_ptr() if bias is not None else None, _bias_dtype(bias),
+            out.data_ptr(), out.stride(0) if M > 0 else N, M, N, K, ws_ptr, ws_bytes, stream)
+    _check(st, "rla_w8a16_gemm")
+    return out
+
+
+def quantize_per_channel(weight: torch.Tensor):
+    """Device per-channel quantization through ``rla_quantize_per_channel``."""
+    lib = load_library()
+    dt = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}.get(weight.dtype)
+    if dt is None:
+        raise TypeError(f"quantize_per_channel: unsupported dtype {weight.dtype}")
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    N, K = w.shape
+    q = torch.empty((N, K), dtype=torch.int8, device=w.device)
+    s = torch.empty((N,), dtype=torch.float32, device=w.device)
+    stream = torch.cuda.current_stream(w.device).cuda_stream
+    with torch.cuda.device(w.device):
+        st = lib.rla_quantize_per_channel(w.data_ptr(), dt, w.stride(0) if N > 0 else K, N, K, q.data_ptr(),
+                                          K, s.data_ptr(), stream)
+    _check(st, "rla_quantize_per_channel")
+    return q, s
+
+
+def gather_columns(staging: torch.Tensor, world: int, M: int, n_local: int, out: torch.Tensor) -> torch.Tensor:
+    """``staging[world, M, n_local]`` -> ``out[M, world * n_local]``."""
+    lib = load_library()
+    stream = torch.cuda.current_stream(out.device).cuda_stream
+    with torch.cuda.device(out.device):
+        st = lib.rla_gather_columns(staging.data_ptr(), world, M, n_local, out.data_ptr(), out.stride(0), stream)
+    _check(st, "rla_gather_columns")
+    return out
+
+
+def launch_count() -> int:
+    return int(load_library().rla_launch_count())
+
+
+def device_error() -> int:
+    """Read and clear the device-side error word (synchronises)."""
+    code = ctypes.c_uint(0)
+    _check(load_library().rla_get_device_error(ctypes.byref(code)), "rla_get_device_error")
+    return int(code.value)

@@ -1,0 +1,71 @@
+"""Build the sm_100a W8A16 library in-tree.
+
+    python -m rotalabs_accel_b200.build        (or __graft_entry__.build())
+
+Compiles ``csrc/rla_lib.cu`` (one translation unit holding every kernel and
+the C ABI of ``include/rla_w8a16.h``) with nvcc for ``sm_100a`` into
+``rotalabs_accel_b200/librla_w8a16.so``.  The CUDA runtime is linked
+statically; the driver's tensor-map encoder is reached through
+``cudaGetDriverEntryPoint`` so nothing links ``libcuda`` directly.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+LIB_NAME = "librla_w8a16.so"
+LIB_PATH = os.path.join(HERE, LIB_NAME)
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "-shared", "-cudart", "static",
+    "--expt-relaxed-constexpr",
+]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found: the sm_100a library cannot be built")
+
+
+def _sources():
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC)
+                  if f.endswith((".cu", ".cuh", ".h"))) + \
+        [os.path.join(os.path.dirname(HERE), "include", "rla_w8a16.h")]
+
+
+def needs_build() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return True
+    t = os.path.getmtime(LIB_PATH)
+    return any(os.path.getmtime(s) > t for s in _sources())
+
+
+def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
+    """Compile the library if a source is newer than it; return its path."""
+    if not force and not needs_build():
+        return LIB_PATH
+    tmp = LIB_PATH + ".tmp"
+    cmd = [_nvcc(), *NVCC_FLAGS, *(extra_flags or []), os.path.join(CSRC, "rla_lib.cu"), "-o", tmp]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    if verbose and (r.stdout or r.stderr):
+        print(r.stdout, r.stderr, file=sys.stderr)
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,241 @@
+// C ABI entry points and the per-shape kernel selector.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <atomic>
+
+#include "rla_internal.h"
+
+namespace rla {
+cudaError_t launch_quantize(const void* w, int w_dtype, int64_t ldw, int64_t N, int64_t K, int8_t* q, int64_t ldq,
+                            float* scale, cudaStream_t s);
+cudaError_t launch_gather(const void* staging, int64_t world, int64_t M, int64_t nl, void* y, int64_t ldy,
+                          cudaStream_t s);
+
+static std::atomic<uint64_t> g_launches{0};
+static thread_local char g_err[512] = "";
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+static constexpr int kNumSMs = 148;  // B200; refined from the device at run time
+
+static int device_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kNumSMs;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return kNumSMs;
+  return n;
+}
+
+// ---------------------------------------------------------------------------
+// The selector.  Static rules keyed on (M, N, K); no run-time autotuning.
+//
+// Skinny kernel (M <= 32): the weight stream is the whole cost, so the plan
+// aims at enough independent 16-byte loads in flight on every SM
+// (Little's law: ~6.5 TB/s x ~1 us => several MB in flight machine-wide).
+// A CTA is 8 warps; rows per CTA and k-slicing are picked so there are at
+// least ~2 CTAs per SM, and split-K across CTAs is added only when the row
+// blocks alone cannot fill the machine (narrow N, e.g. a column shard).
+//
+// tcgen05 kernel (M > 32): tile 128 weight rows x BM tokens; BM = 256 for
+// long prefills, smaller for mid-size M so that the grid covers the SMs.
+// ---------------------------------------------------------------------------
+static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws, int sms) {
+  p.kernel = RLA_KERNEL_SKINNY;
+  p.nt = M <= 8 ? 1 : M <= 16 ? 2 : 4;
+  const int64_t chunks = (K + 63) / 64;
+  // Prefer more rows per CTA when K is short (fewer chunks to spread over warps).
+  if (chunks >= 64) {
+    p.wn = 1; p.wk = 8;
+  } else if (chunks >= 16) {
+    p.wn = 2; p.wk = 4;
+  } else {
+    p.wn = 4; p.wk = 2;
+  }
+  const int rows = 16 * p.wn;
+  p.grid_x = static_cast<int>((N + rows - 1) / rows);
+  p.splits = 1;
+  const int64_t target_ctas = 2LL * sms;
+  if (have_ws && p.grid_x < target_ctas && p.grid_x <= kMaxSplitRowBlocks) {
+    // Each CTA slice should still give every k-warp a few chunks.
+    const int64_t max_splits = chunks / (2 * p.wk);
+    int64_t s = (target_ctas + p.grid_x - 1) / p.grid_x;
+    if (s > max_splits) s = max_splits;
+    if (s > 32) s = 32;
+    if (s > 1) p.splits = static_cast<int>(s);
+  }
+  p.grid_y = p.splits;
+  p.threads = 32 * p.wn * p.wk;
+  p.smem = 0;
+  if (p.splits > 1) p.workspace = kSplitCounterBytes + (size_t)p.splits * (size_t)M * (size_t)N * 4;
+}
+
+Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace) {
+  Plan p;
+  if (M == 0 || N == 0) return p;
+  if (K == 0) {
+    p.kernel = RLA_KERNEL_FILL;
+    return p;
+  }
+  const int sms = device_sm_count();
+  if (aligned && K % 16 == 0 && M <= 32) {
+    skinny_shape(p, M, N, K, have_workspace, sms);
+    return p;
+  }
+  if (aligned && M > 32) {
+    p.kernel = RLA_KERNEL_TCGEN05;
+    const int64_t ntiles = (N + 127) / 128;
+    if (M >= 256 && ntiles * ((M + 255) / 256) >= sms) {
+      p.bm = 256; p.stages = 4;
+    } else if (M > 64) {
+      p.bm = 128; p.stages = 6;
+    } else {
+      p.bm = 64; p.stages = 8;
+    }
+    p.grid_x = static_cast<int>(ntiles);
+    p.grid_y = static_cast<int>((M + p.bm - 1) / p.bm);
+    p.threads = 192;
+    p.smem = tcgen05_smem_bytes(p.bm, p.stages);
+    return p;
+  }
+  p.kernel = RLA_KERNEL_GENERIC;
+  return p;
+}
+
+}  // namespace rla
+
+using namespace rla;
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int fail(int code, const char* msg) {
+  set_error("%s", msg);
+  return code;
+}
+
+extern "C" {
+
+int rla_version(void) { return 1 * 10000 + 0 * 100 + 0; }
+
+const char* rla_last_error(void) { return g_err; }
+
+uint64_t rla_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int rla_get_device_error(unsigned int* code) {
+  if (!code) return fail(RLA_ERR_INVALID_ARGUMENT, "code is NULL");
+  unsigned int zero = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(code, rla_device_error, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(rla_device_error, &zero, sizeof(unsigned int));
+  if (e != cudaSuccess) {
+    set_error("rla_get_device_error: %s", cudaGetErrorString(e));
+    return RLA_ERR_CUDA;
+  }
+  return RLA_OK;
+}
+
+size_t rla_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N < 0 || K < 0) return 0;
+  return make_plan(M, N, K, true, true).workspace;
+}
+
+int rla_w8a16_plan(int64_t M, int64_t N, int64_t K, int aligned, int have_workspace, int64_t* params) {
+  if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_plan: sizes must be in [0, 2^31)");
+  const Plan p = make_plan(M, N, K, aligned != 0, have_workspace != 0);
+  if (params) {
+    params[0] = p.kernel;
+    params[1] = p.grid_x;
+    params[2] = p.grid_y;
+    params[3] = p.threads;
+    params[4] = p.splits;
+    params[5] = p.kernel == RLA_KERNEL_SKINNY ? 16 * p.wn : p.kernel == RLA_KERNEL_TCGEN05 ? 128 : 0;
+    params[6] = p.kernel == RLA_KERNEL_SKINNY ? 8 * p.nt : p.bm;
+    params[7] = static_cast<int64_t>(p.smem);
+  }
+  return RLA_OK;
+}
+
+int rla_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale, int scale_dtype,
+                   const void* bias, int bias_dtype, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm: M, N, K must be in [0, 2^31)");
+  if (M == 0 || N == 0) return RLA_OK;
+  if (scale_dtype != RLA_DTYPE_F16 && scale_dtype != RLA_DTYPE_F32)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm: scale_dtype must be F16 or F32");
+  if (bias_dtype != RLA_DTYPE_NONE && bias_dtype != RLA_DTYPE_F16 && bias_dtype != RLA_DTYPE_F32)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm: bias_dtype must be NONE, F16 or F32");
+  if (bias_dtype != RLA_DTYPE_NONE && !bias)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm: bias is NULL but bias_dtype is set");
+  if (!y || !scale || (K > 0 && (!x || !w)))
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm: null x, w, scale or y");
+  if (ldy < N || (K > 0 && (ldx < K || ldw < K)))
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm: leading dimensions must be >= the row length");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(RLA_ERR_WORKSPACE, "rla_w8a16_gemm: workspace must be 256-byte aligned");
+
+  GemmArgs a{x, ldx, w, ldw, scale, scale_dtype == RLA_DTYPE_F32 ? 1 : 0, bias,
+             bias_dtype == RLA_DTYPE_NONE ? 0 : bias_dtype == RLA_DTYPE_F16 ? 1 : 2,
+             y, ldy, (int)M, (int)N, (int)K};
+  const bool aligned = aligned16(x) && aligned16(w) && (ldx % 8 == 0) && (ldw % 16 == 0);
+  Plan p = make_plan(M, N, K, aligned, workspace != nullptr && workspace_bytes > 0);
+  if (p.workspace > workspace_bytes) p = make_plan(M, N, K, aligned, false);  // too small: no split-K
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  switch (p.kernel) {
+    case RLA_KERNEL_SKINNY: e = launch_skinny(a, p, workspace, s); break;
+    case RLA_KERNEL_TCGEN05: e = launch_tcgen05(a, p, s); break;
+    case RLA_KERNEL_GENERIC: e = launch_generic(a, s); break;
+    case RLA_KERNEL_FILL: e = launch_fill(a, s); break;
+    default: return RLA_OK;
+  }
+  if (e != cudaSuccess) {
+    set_error("rla_w8a16_gemm: launch of kernel family %d failed: %s", p.kernel, cudaGetErrorString(e));
+    return RLA_ERR_CUDA;
+  }
+  note_launch();
+  return RLA_OK;
+}
+
+int rla_quantize_per_channel(const void* w, int w_dtype, int64_t ldw, int64_t N, int64_t K, int8_t* q,
+                             int64_t ldq, float* scale, void* stream) {
+  if (N < 0 || K < 0 || N > INT32_MAX || K > INT32_MAX)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_quantize_per_channel: sizes must be in [0, 2^31)");
+  if (N == 0) return RLA_OK;
+  if (!w || !q || !scale) return fail(RLA_ERR_INVALID_ARGUMENT, "rla_quantize_per_channel: null pointer");
+  if (w_dtype != RLA_DTYPE_F32 && w_dtype != RLA_DTYPE_F16 && w_dtype != RLA_DTYPE_BF16)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_quantize_per_channel: w_dtype must be F32, F16 or BF16");
+  if (ldw < K || ldq < K) return fail(RLA_ERR_INVALID_ARGUMENT, "rla_quantize_per_channel: bad leading dimension");
+  cudaError_t e = launch_quantize(w, w_dtype, ldw, N, K, q, ldq, scale, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("rla_quantize_per_channel: %s", cudaGetErrorString(e));
+    return RLA_ERR_CUDA;
+  }
+  note_launch();
+  return RLA_OK;
+}
+
+int rla_gather_columns(const void* staging, int64_t world, int64_t M, int64_t n_local, void* y, int64_t ldy,
+                       void* stream) {
+  if (world < 1 || M < 0 || n_local < 0 || ldy < world * n_local)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_gather_columns: bad sizes");
+  if (M == 0 || n_local == 0) return RLA_OK;
+  if (!staging || !y) return fail(RLA_ERR_INVALID_ARGUMENT, "rla_gather_columns: null pointer");
+  cudaError_t e = launch_gather(staging, world, M, n_local, y, ldy, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("rla_gather_columns: %s", cudaGetErrorString(e));
+    return RLA_ERR_CUDA;
+  }
+  note_launch();
+  return RLA_OK;
+}
+
+}  // extern "C"

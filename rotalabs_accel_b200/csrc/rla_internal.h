@@ -1,0 +1,63 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/rla_w8a16.h"
+
+namespace rla {
+
+// Arguments common to every W8A16 GEMM kernel.
+struct GemmArgs {
+  const void* x;
+  int64_t ldx;
+  const int8_t* w;
+  int64_t ldw;
+  const void* scale;
+  int scale_f32;  // 1: fp32 scale, 0: fp16 scale
+  const void* bias;
+  int bias_kind;  // 0 none, 1 fp16, 2 fp32
+  void* y;
+  int64_t ldy;
+  int M, N, K;
+};
+
+// A launch plan chosen by the per-shape selector.
+struct Plan {
+  int kernel = RLA_KERNEL_NONE;
+  // skinny kernel
+  int nt = 0;      // 8-row tiles of x per MMA column block (M <= 8 * nt)
+  int wn = 0;      // 16-row groups of w per CTA
+  int wk = 0;      // k-slicing warps per CTA
+  int splits = 1;  // CTAs along K (split-K across CTAs when > 1)
+  // tcgen05 kernel
+  int bm = 0;      // rows of x per tile (MMA N)
+  int stages = 0;  // TMA pipeline depth
+  // common
+  int grid_x = 0, grid_y = 0, threads = 0;
+  size_t smem = 0;
+  size_t workspace = 0;
+};
+
+// Split-K workspace layout (fixed, so calls with different shapes can share
+// one workspace): [0, kSplitCounterBytes) arrival counters, one per row
+// block, zero between calls; then the fp32 partial sums [splits][M][N].
+constexpr size_t kSplitCounterBytes = 4096;
+constexpr int kMaxSplitRowBlocks = static_cast<int>(kSplitCounterBytes / sizeof(unsigned int));
+
+Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace);
+
+void note_launch();
+void set_error(const char* fmt, ...);
+
+cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
+cudaError_t launch_tcgen05(const GemmArgs& a, const Plan& p, cudaStream_t s);
+cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s);
+cudaError_t launch_fill(const GemmArgs& a, cudaStream_t s);
+
+size_t tcgen05_smem_bytes(int bm, int stages);
+int tcgen05_tmem_cols(int bm);
+
+}  // namespace rla

@@ -1,0 +1,6 @@
+// The whole library as one translation unit (no relocatable device code is
+// needed for the shared device-side error word).
+#include "rla_misc.cu"
+#include "rla_skinny.cu"
+#include "rla_tc.cu"
+#include "rla_capi.cu"

@@ -1,0 +1,236 @@
+// Decode-regime W8A16 kernel (M <= 32): stream the int8 weight once from HBM.
+//
+// Work split.  A CTA owns 16*WN consecutive weight rows (output channels n)
+// and one slice of K (split-K across CTAs when gridDim.y > 1).  Inside the
+// CTA, warp (wn, wk) owns rows [16*wn, 16*wn + 16) and every WK-th 64-wide
+// chunk of the CTA's K slice.  Partial sums of the WK warps are added in
+// shared memory in a fixed order; partial sums of the CTAs along K go
+// through the caller's workspace and are added, again in a fixed order, by
+// whichever CTA of the row block finishes last.  Results are therefore
+// bit-reproducible from run to run.
+//
+// Inner product on the tensor cores, "swap-AB": the weight rows are the MMA
+// rows (m16) and the <= 8*NT activation rows are the MMA columns (n8), so a
+// 16x8x16 MMA carries 16 output channels of up to 8 tokens.  Because a dot
+// product does not care in which order its k terms are visited, each lane
+// loads 16 *contiguous* weight bytes per row with one 128-bit load and the
+// k order inside the MMA fragment is permuted to match; the activation
+// fragment is loaded with the same permutation (32 contiguous bytes of x).
+// Lane (g = lane/4, q = lane%4) of a chunk starting at kb covers
+// k in [kb + 16q, kb + 16q + 16) for weight rows g and g+8 and x row g:
+//   MMA step s (0..3), fragment k columns {2q, 2q+1} <- k = kb+16q+4s+{0,1}
+//                                         {2q+8, 2q+9} <- k = kb+16q+4s+{2,3}
+// int8 -> fp16 happens in registers (rla_i8x4_to_h2x2).
+#include "rla_common.cuh"
+#include "rla_internal.h"
+
+namespace rla {
+
+template <int NT>
+struct XFrag {
+  uint4 v[NT][2];
+};
+
+template <int NT, int WN, int WK, int U>
+__global__ void __launch_bounds__(32 * WN * WK)
+    w8a16_skinny_kernel(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,
+                        const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias,
+                        int bias_kind, __half* __restrict__ y, int64_t ldy, int M, int N, int K,
+                        int chunks_per_split, float* __restrict__ partial, unsigned int* __restrict__ counters) {
+  constexpr int ROWS = 16 * WN;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int wn = warp % WN;
+  const int wk = warp / WN;
+  const int g = lane >> 2;
+  const int q = lane & 3;
+
+  const int row_base = blockIdx.x * ROWS;
+  const int n0 = row_base + wn * 16;
+  const int r0 = min(n0 + g, N - 1);
+  const int r1 = min(n0 + g + 8, N - 1);
+  const int8_t* wrow0 = w + (int64_t)r0 * ldw + q * 16;
+  const int8_t* wrow1 = w + (int64_t)r1 * ldw + q * 16;
+
+  bool xrow_ok[NT];
+  const __half* xrow[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const int xr = t * 8 + g;
+    xrow_ok[t] = xr < M;
+    xrow[t] = x + (int64_t)(xrow_ok[t] ? xr : 0) * ldx + q * 16;
+  }
+
+  const int total_chunks = (K + 63) >> 6;
+  const int c_begin = blockIdx.y * chunks_per_split;
+  const int c_end = min(total_chunks, c_begin + chunks_per_split);
+
+  float acc[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+
+  const uint4 zero4 = make_uint4(0, 0, 0, 0);
+  for (int c = c_begin + wk; c < c_end; c += WK * U) {
+    uint4 wa[U][2];
+    XFrag<NT> xb[U];
+    // Issue every load of U chunks before any math: U*2 streaming 16-byte
+    // weight loads (plus the L1-resident activation loads) in flight per lane.
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int cc = c + u * WK;
+      const int kofs = cc * 64;
+      const bool ok = (cc < c_end) && (kofs + q * 16 < K);
+      wa[u][0] = ok ? rla_ldg_stream(wrow0 + kofs) : zero4;
+      wa[u][1] = ok ? rla_ldg_stream(wrow1 + kofs) : zero4;
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const bool okx = ok && xrow_ok[t];
+        xb[u].v[t][0] = okx ? rla_ldg_keep(xrow[t] + kofs) : zero4;
+        xb[u].v[t][1] = okx ? rla_ldg_keep(xrow[t] + kofs + 8) : zero4;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t* w0 = reinterpret_cast<const uint32_t*>(&wa[u][0]);
+      const uint32_t* w1 = reinterpret_cast<const uint32_t*>(&wa[u][1]);
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        uint32_t a0, a1, a2, a3;
+        rla_i8x4_to_h2x2(w0[s], a0, a2);  // row g:   k {2q,2q+1} and {2q+8,2q+9}
+        rla_i8x4_to_h2x2(w1[s], a1, a3);  // row g+8
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xb[u].v[t][0]);
+          rla_mma_16816(acc[t], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
+        }
+      }
+    }
+  }
+
+  // ---- reduce the WK k-slicing warps (fixed order) ----
+  __shared__ float red[(WK > 1 ? WK - 1 : 1) * WN * NT * 4 * 32];
+  if constexpr (WK > 1) {
+    if (wk > 0) {
+      float* dst = red + (((wk - 1) * WN + wn) * NT * 4) * 32;
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[(t * 4 + i) * 32 + lane] = acc[t][i];
+    }
+    __syncthreads();
+    if (wk == 0) {
+      for (int j = 0; j < WK - 1; ++j) {
+        const float* src = red + ((j * WN + wn) * NT * 4) * 32;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[t][i] += src[(t * 4 + i) * 32 + lane];
+      }
+    }
+  }
+
+  // Accumulator element (t, i): row n = n0 + g + 8*(i>>1), token m = 8t + 2q + (i&1).
+  if (gridDim.y == 1) {
+    if (wk == 0) {
+#pragma unroll
+      for (int hi = 0; hi < 2; ++hi) {
+        const int n = n0 + g + 8 * hi;
+        if (n >= N) continue;
+        const float sc = scale_f32 ? static_cast<const float*>(scale)[n]
+                                   : __half2float(static_cast<const __half*>(scale)[n]);
+        const float bi = bias_kind == 0 ? 0.f
+                         : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias)[n])
+                                          : static_cast<const float*>(bias)[n];
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = t * 8 + 2 * q + j;
+            if (m < M) y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(acc[t][2 * hi + j], sc, bi));
+          }
+      }
+    }
+    return;
+  }
+
+  // ---- split-K across CTAs: publish this slice, the last CTA adds them all ----
+  if (wk == 0) {
+    float* part = partial + (int64_t)blockIdx.y * M * N;
+#pragma unroll
+    for (int hi = 0; hi < 2; ++hi) {
+      const int n = n0 + g + 8 * hi;
+      if (n >= N) continue;
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int m = t * 8 + 2 * q + j;
+          if (m < M) __stcg(part + (int64_t)m * N + n, acc[t][2 * hi + j]);
+        }
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int is_last;
+  if (threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(counters + blockIdx.x, 1u);
+    is_last = (prev == gridDim.y - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  const int rows_here = min(ROWS, N - row_base);
+  for (int idx = threadIdx.x; idx < rows_here * M; idx += blockDim.x) {
+    const int n = row_base + idx % rows_here;
+    const int m = idx / rows_here;
+    float sum = 0.f;
+    for (int sidx = 0; sidx < (int)gridDim.y; ++sidx) sum += __ldcg(partial + ((int64_t)sidx * M + m) * N + n);
+    const float sc =
+        scale_f32 ? static_cast<const float*>(scale)[n] : __half2float(static_cast<const __half*>(scale)[n]);
+    const float bi = bias_kind == 0 ? 0.f
+                     : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias)[n])
+                                      : static_cast<const float*>(bias)[n];
+    y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(sum, sc, bi));
+  }
+  if (threadIdx.x == 0) counters[blockIdx.x] = 0u;  // leave the workspace re-usable
+}
+
+template <int NT, int WN, int WK, int U>
+static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s) {
+  const int total_chunks = (a.K + 63) / 64;
+  const int cps = (total_chunks + p.splits - 1) / p.splits;
+  unsigned int* counters = nullptr;
+  float* partial = nullptr;
+  if (p.splits > 1) {
+    counters = static_cast<unsigned int*>(workspace);
+    partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kSplitCounterBytes);
+  }
+  dim3 grid(p.grid_x, p.splits);
+  w8a16_skinny_kernel<NT, WN, WK, U><<<grid, 32 * WN * WK, 0, s>>>(
+      static_cast<const __half*>(a.x), a.ldx, a.w, a.ldw, a.scale, a.scale_f32, a.bias, a.bias_kind,
+      static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K, cps, partial, counters);
+  return cudaGetLastError();
+}
+
+// Instantiated configurations: NT in {1, 2, 4}; (WN, WK) in {(1, 8), (2, 4), (4, 2)}.
+template <int NT>
+static cudaError_t launch_nt(const GemmArgs& a, const Plan& p, void* ws, cudaStream_t s) {
+  constexpr int U = NT >= 4 ? 2 : 4;
+  if (p.wn == 1 && p.wk == 8) return launch_cfg<NT, 1, 8, U>(a, p, ws, s);
+  if (p.wn == 2 && p.wk == 4) return launch_cfg<NT, 2, 4, U>(a, p, ws, s);
+  if (p.wn == 4 && p.wk == 2) return launch_cfg<NT, 4, 2, U>(a, p, ws, s);
+  if (p.wn == 1 && p.wk == 4) return launch_cfg<NT, 1, 4, U>(a, p, ws, s);
+  return cudaErrorInvalidConfiguration;
+}
+
+cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s) {
+  switch (p.nt) {
+    case 1: return launch_nt<1>(a, p, workspace, s);
+    case 2: return launch_nt<2>(a, p, workspace, s);
+    case 4: return launch_nt<4>(a, p, workspace, s);
+    default: return cudaErrorInvalidConfiguration;
+  }
+}
+
+}  // namespace rla

@@ -1,0 +1,111 @@
+"""The C-ABI library on a CPU-only host: it loads, exports every symbol
+``include/*.h`` declares, and its host-side logic (argument validation, the
+per-shape selector, workspace sizing) behaves.  No compute call is made.
+"""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from rotalabs_accel_b200 import _capi, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _capi.load_library()
+
+
+def _declared_symbols():
+    syms = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        syms |= set(re.findall(r"RLA_API\s+[\w\s\*]+?\b(rla_\w+)\s*\(", text))
+    return syms
+
+
+def test_header_declares_the_abi():
+    syms = _declared_symbols()
+    assert {"rla_w8a16_gemm", "rla_w8a16_workspace_size", "rla_w8a16_plan", "rla_quantize_per_channel",
+            "rla_gather_columns", "rla_launch_count", "rla_get_device_error", "rla_last_error",
+            "rla_version"} <= syms
+    assert set(_capi.EXPORTED_SYMBOLS) <= syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for sym in _declared_symbols():
+        assert hasattr(lib, sym), f"{sym} declared in include/ but not exported"
+    assert lib.rla_version() == 10000
+
+
+def test_library_is_sm100a_only():
+    # the fatbin holds sm_100a code only (no PTX / other archs): check the build flags
+    assert "arch=compute_100a,code=sm_100a" in " ".join(build.NVCC_FLAGS)
+
+
+def test_invalid_arguments_are_rejected_without_launch(lib):
+    n0 = lib.rla_launch_count()
+    p = ctypes.c_void_p(16)   # never dereferenced: validation fails first
+    # negative size
+    assert lib.rla_w8a16_gemm(p, 64, p, 64, p, 1, None, 0, p, 64, -1, 64, 64, None, 0, None) == 1
+    # bad scale dtype
+    assert lib.rla_w8a16_gemm(p, 64, p, 64, p, 7, None, 0, p, 64, 4, 64, 64, None, 0, None) == 1
+    # bias dtype set but NULL bias
+    assert lib.rla_w8a16_gemm(p, 64, p, 64, p, 1, None, 1, p, 64, 4, 64, 64, None, 0, None) == 1
+    # leading dimension too small
+    assert lib.rla_w8a16_gemm(p, 32, p, 64, p, 1, None, 0, p, 64, 4, 64, 64, None, 0, None) == 1
+    # misaligned workspace
+    assert lib.rla_w8a16_gemm(p, 64, p, 64, p, 1, None, 0, p, 64, 4, 64, 64, ctypes.c_void_p(8), 64, None) == 4
+    assert b"workspace" in lib.rla_last_error()
+    # empty problems are a no-op success
+    assert lib.rla_w8a16_gemm(None, 0, None, 0, p, 1, None, 0, p, 0, 0, 64, 64, None, 0, None) == 0
+    assert lib.rla_w8a16_gemm(None, 0, None, 0, p, 1, None, 0, p, 0, 4, 0, 64, None, 0, None) == 0
+    assert lib.rla_quantize_per_channel(p, 9, 8, 4, 8, p, 8, p, None) == 1
+    assert lib.rla_gather_columns(p, 0, 1, 1, p, 1, None) == 1
+    assert lib.rla_launch_count() == n0
+
+
+def test_selector_rules(lib):
+    # decode regime -> the skinny HBM-streaming kernel
+    for M in (1, 4, 8, 16, 32):
+        for K, N in ((4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336)):
+            p = _capi.plan(M, N, K)
+            assert p["kernel_name"] == "skinny"
+            assert p["x_rows"] >= M and p["x_rows"] <= 32
+            assert p["grid_x"] * p["w_rows"] >= N
+    # narrow column shards with long K get split-K across CTAs
+    p = _capi.plan(1, 1024, 28672)
+    assert p["kernel_name"] == "skinny" and p["splits"] > 1
+    assert _capi.plan(1, 1024, 28672, have_workspace=False)["splits"] == 1
+    # prefill regime -> tcgen05
+    for K, N in ((4096, 12288), (4096, 11008), (11008, 4096)):
+        p = _capi.plan(2048, N, K)
+        assert p["kernel_name"] == "tcgen05" and p["w_rows"] == 128
+        assert p["grid_x"] * 128 >= N and p["grid_y"] * p["x_rows"] >= 2048
+        assert p["smem"] <= 227 * 1024
+    # unaligned / ragged -> generic; K == 0 -> fill; empty -> none
+    assert _capi.plan(4, 64, 64, aligned=False)["kernel_name"] == "generic"
+    assert _capi.plan(4, 64, 40)["kernel_name"] == "generic"        # K % 16 != 0 on the skinny path
+    assert _capi.plan(4, 64, 0)["kernel_name"] == "fill"
+    assert _capi.plan(0, 64, 64)["kernel_name"] == "none"
+
+
+def test_workspace_size(lib):
+    assert lib.rla_w8a16_workspace_size(2048, 4096, 4096) == 0
+    p = _capi.plan(1, 1024, 28672)
+    need = lib.rla_w8a16_workspace_size(1, 1024, 28672)
+    assert need >= p["splits"] * 1 * 1024 * 4
+    assert need % 4 == 0
+
+
+def test_cuda_path_never_falls_back(monkeypatch):
+    """If the library cannot be loaded, the CUDA path raises; it never
+    computes CUDA tensors another way."""
+    monkeypatch.setattr(_capi, "_lib", None)
+    with pytest.raises(RuntimeError, match="missing"):
+        _capi.load_library("/nonexistent/librla_w8a16.so")
