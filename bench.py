@@ -1,0 +1,456 @@
+"""Benchmark of the W8A16 GEMM path on B200 (one JSON line on rank 0).
+
+Workload (a "step"): the decode GEMV sweep of the benchmark configuration --
+M in {1, 4, 8, 16} x (K, N) in {(4096, 4096), (4096, 11008), (11008, 4096),
+(4096, 14336)}: 16 W8A16 GEMMs, each with its own int8 weight (663 MB of
+weights in all, > the 126 MB L2, so every GEMM streams its weight from HBM).
+x ~ N(0, 1) fp16, W ~ N(0, 0.02) quantized per output channel, fp16 scales,
+seeded synthetic data.  With N GPUs every layer is column-parallel: each
+rank holds N_layer / world output channels, runs its slice and the slices
+are all-gathered over NCCL and reassembled (strong scaling).
+
+Reported (rank 0, one line):
+  value      algorithmic bytes of the whole sweep (sum of N*K + 2MK + 2N + 2MN
+             over the 16 GEMMs) / device time per step, TB/s; steps replay a
+             CUDA graph of the step; device time is CUDA events on the replay
+             stream, max over ranks.
+  e2e        the same metric through the public API (``int8_gemm`` /
+             ``ColumnParallelInt8Linear``), eager, with every step's x copied
+             host->device from pinned memory and every y copied back.
+  roofline   the decode kernel: bytes per launch / its average launch time,
+             against the measured HBM copy bandwidth.
+  prefill    (N=1) the M=2048 prefill GEMMs of the benchmark configuration,
+             TFLOP/s, against the measured dense bf16/fp16 tensor peak.
+  cpu_baseline  the CPU oracle (rotalabs-accel's CPU algorithm restated in
+             numpy) on one pass of the sweep, on this host's cores.
+
+``--impl reference`` times rotalabs-accel's own CPU path (its algorithm
+restated as the oracle; rotalabs-accel is Python, nothing compiles) on the
+same workload and metric, one GEMM of the sweep per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DECODE_MS = (1, 4, 8, 16)
+DECODE_KN = ((4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336))
+PREFILL_M = 2048
+PREFILL_KN = ((4096, 12288), (4096, 11008), (11008, 4096))
+METRIC = "W8A16 GEMM achieved TB/s (decode M<=16) and TFLOPS (prefill M=2048) vs B200 roofline"
+
+
+def sweep():
+    return [(M, K, N) for M in DECODE_MS for (K, N) in DECODE_KN]
+
+
+def gemm_bytes(M, K, N):
+    return N * K + 2 * M * K + 2 * N + 2 * M * N
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the decode kernel over the sweep, from the
+    committed ncu summary (profiles/skinny_decode_sweep.md)."""
+    p = os.path.join(ROOT, "profiles", "skinny_decode_sweep.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch"):
+            try:
+                return float(line.split("=")[1].split()[0])
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (oracle: the reference's CPU algorithm restated in numpy)
+# ---------------------------------------------------------------------------
+def _cpu_problem(M, K, N, seed):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    from oracle import w8a16_oracle as orc
+    q, s = orc.quantize_weight_per_channel(w)
+    return x, q, s.astype(np.float16)
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def time_cpu_gemm(M, K, N, seed, threads):
+    from oracle import w8a16_oracle as orc
+    x, q, s = _cpu_problem(M, K, N, seed)
+    t0 = time.perf_counter()
+    orc.int8_gemm_parallel(x, q, s, threads=threads)
+    return time.perf_counter() - t0
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (oracle port), one GEMM of the
+    sweep per step, all host threads."""
+    threads = cpu_threads()
+    jobs = sweep()
+    # Each step is one GEMM of the sweep; the run is bounded in wall time so
+    # that the GPU arm's --steps (thousands) still ends within minutes.
+    budget_s, t_start = 120.0, time.perf_counter()
+    for i in range(min(args.warmup, 3)):
+        M, K, N = jobs[i % len(jobs)]
+        time_cpu_gemm(M, K, N, 1000 + i, threads)
+    tot_b, tot_t, done = 0, 0.0, []
+    for i in range(args.steps):
+        if i >= len(jobs) and time.perf_counter() - t_start > budget_s:
+            break
+        M, K, N = jobs[i % len(jobs)]
+        tot_t += time_cpu_gemm(M, K, N, i, threads)
+        tot_b += gemm_bytes(M, K, N)
+        done.append(f"{M}x{K}x{N}")
+    value = tot_b / tot_t / 1e12
+    line = {"metric": METRIC, "value": round(value, 6), "unit": "TB/s", "n_gpus": args.gpus, "steps": len(done),
+            "steps_requested": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(tot_t / len(done) * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (int8 weights)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "decode GEMV sweep (BASELINE config 1), one GEMM per step",
+                       "sweep": "M in {1,4,8,16} x (K,N) in {(4096,4096),(4096,11008),(11008,4096),(4096,14336)}",
+                       "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(value, 6), "unit": "TB/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} GEMMs of the sweep ({', '.join(done[:16])}{'...' if len(done) > 16 else ''}); "
+                                       "rotalabs-accel's CPU algorithm (dequantize the whole weight to fp16, "
+                                       "then fp32-accumulated linear) restated in numpy (oracle/w8a16_oracle.py)"},
+            "e2e": {"value": round(value, 6), "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    import rotalabs_accel_b200 as ra
+    from rotalabs_accel_b200 import _capi
+    from rotalabs_accel_b200.sharded import ColumnParallelInt8Linear, assemble_columns, shard_range
+
+    peaks = load_peaks()
+
+    # ---- workload: every rank holds its column shard of every layer ----
+    jobs = sweep()
+    layers = []
+    for i, (M, K, N) in enumerate(jobs):
+        g = torch.Generator(device=dev).manual_seed(1000 + i)
+        x = torch.randn(M, K, generator=g, device=dev).half()
+        w_full = torch.randn(N, K, generator=g, device=dev) * 0.02
+        start, stop, n_local = shard_range(N, world, rank)
+        q, s = ra.quantize_weight_per_channel(w_full[start:stop])
+        del w_full
+        s = s.half()
+        y_local = torch.empty(M, n_local, device=dev, dtype=torch.float16)
+        staging = torch.empty(world, M, n_local, device=dev, dtype=torch.float16) if world > 1 else None
+        y = torch.empty(M, N, device=dev, dtype=torch.float16)
+        layers.append(dict(M=M, K=K, N=N, x=x, q=q, s=s, y_local=y_local, staging=staging, y=y, n_local=n_local))
+    torch.cuda.synchronize()
+    bytes_step = sum(gemm_bytes(M, K, N) for (M, K, N) in jobs)
+
+    stream = torch.cuda.Stream(device=dev)
+
+    def gemm_only():
+        for L in layers:
+            _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y_local"] if world > 1 else L["y"])
+
+    def step():
+        for L in layers:
+            if world == 1:
+                _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y"])
+            else:
+                _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y_local"])
+                dist.all_gather_into_tensor(L["staging"], L["y_local"])
+                assemble_columns(L["staging"], L["N"], out=L["y"])
+
+    def capture(fn):
+        with torch.cuda.stream(stream):
+            fn()   # warm (allocates the split-K workspace for this stream)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        return g
+
+    def timed(graph, steps, warmup, sample_clocks=False):
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        sampler = ClockSampler(local_rank) if sample_clocks else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        clocks = sampler.stop() if sampler else None
+        if world > 1:
+            dist.barrier()
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms, clocks
+
+    launches_per_step = len(layers) * (1 if world == 1 else 2)   # GEMM (+ gather kernel; M=1 uses a copy)
+    if world > 1:
+        launches_per_step = len(layers) + sum(1 for L in layers if L["M"] > 1)
+
+    g_step = capture(step)
+    ms_step, clocks = timed(g_step, args.steps, args.warmup, sample_clocks=(rank == 0))
+    value = bytes_step / (ms_step * 1e-3) / 1e12
+
+    # ---- the decode kernel alone (roofline) ----
+    if world == 1:
+        ms_gemm = ms_step
+        g_gemm = None
+    else:
+        g_gemm = capture(gemm_only)
+        ms_gemm, _ = timed(g_gemm, max(100, args.steps // 4), args.warmup)
+    local_bytes = sum(gemm_bytes(L["M"], L["K"], L["n_local"]) for L in layers)
+    avg_launch_us = ms_gemm * 1e3 / len(layers)
+    achieved = local_bytes / len(layers) / (avg_launch_us * 1e-6) / 1e9
+    traffic = load_traffic() if world == 1 else None
+
+    # ---- end to end through the public API, host buffers ----
+    torch.cuda.synchronize()
+    xs_host = [L["x"].cpu().pin_memory() for L in layers]
+    ys_host = [torch.empty(L["M"], L["N"], dtype=torch.float16).pin_memory() for L in layers]
+    mods = []
+    for L in layers:
+        if world > 1:
+            m = ColumnParallelInt8Linear(L["K"], L["N"]).to(dev)
+            m.weight_int8.copy_(L["q"])
+            m.scale.copy_(L["s"].float())
+            m._quantized = True
+        else:
+            m = ra.Int8Linear(L["K"], L["N"])
+            m.weight_int8 = L["q"]
+            m.scale = L["s"]
+            m.weight_transposed = torch.empty(0, dtype=torch.int8, device=dev)
+            m._quantized = True
+        mods.append(m)
+    h2d = sum(t.numel() * 2 for t in xs_host)
+    d2h = sum(t.numel() * 2 for t in ys_host)
+
+    def e2e_step():
+        for m, xh, yh in zip(mods, xs_host, ys_host):
+            xd = xh.to(dev, non_blocking=True)
+            yd = m(xd)
+            yh.copy_(yd, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = t.item()
+    e2e_value = bytes_step / (ms_e2e * 1e-3) / 1e12
+
+    # ---- prefill (N = 1) ----
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        pl = []
+        for i, (K, N) in enumerate(PREFILL_KN):
+            g = torch.Generator(device=dev).manual_seed(2000 + i)
+            x = torch.randn(PREFILL_M, K, generator=g, device=dev).half()
+            q, s = ra.quantize_weight_per_channel(torch.randn(N, K, generator=g, device=dev) * 0.02)
+            pl.append((x, q, s.half(), torch.empty(PREFILL_M, N, device=dev, dtype=torch.float16)))
+
+        def pstep():
+            for (x, q, s, y) in pl:
+                _capi.w8a16_gemm(x, q, s, None, out=y)
+        g_pre = capture(pstep)
+        pre_steps = max(20, args.steps // 10)
+        ms_pre, pclocks = timed(g_pre, pre_steps, args.warmup, sample_clocks=(rank == 0))
+        flops = sum(2 * PREFILL_M * N * K for (K, N) in PREFILL_KN)
+        tflops = flops / (ms_pre * 1e-3) / 1e12
+        prefill = {"value": round(tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(ms_pre, 4),
+                   "steps": pre_steps, "gemms": [f"{PREFILL_M}x{K}->{N}" for (K, N) in PREFILL_KN],
+                   "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["bf16_tflops"],
+                                "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4),
+                                "peak_kind": f"dense bf16/fp16 burst ({peaks['source']})", "traffic": None},
+                   "clocks": pclocks}
+        del g_pre
+
+    # ---- CPU baseline (rank 0, N = 1) ----
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        threads = cpu_threads()
+        t_cpu, b_cpu = 0.0, 0
+        for i, (M, K, N) in enumerate(jobs):
+            t_cpu += time_cpu_gemm(M, K, N, i, threads)
+            b_cpu += gemm_bytes(M, K, N)
+        cpu = {"value": round(b_cpu / t_cpu / 1e12, 6), "unit": "TB/s", "cores": threads, "kind": "port",
+               "sample": f"one pass of the 16-GEMM decode sweep ({t_cpu:.1f} s): rotalabs-accel's CPU algorithm "
+                         "(whole-weight dequantize to fp16, then fp32-accumulated linear) restated in numpy"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (int8 weights, fp32 accumulate)",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) per-channel int8 weights)",
+            "config": {"workload": "decode GEMV sweep, BASELINE config 1: M in {1,4,8,16} x (K,N) in "
+                                   "{(4096,4096),(4096,11008),(11008,4096),(4096,14336)}, 16 GEMMs per step",
+                       "parallelism": "single GPU" if world == 1 else
+                       f"column-parallel over {world} GPUs + NCCL all-gather of each output",
+                       "weights_bytes": sum(L["q"].numel() for L in layers) * world,
+                       "l2": "working set > L2: each GEMM has its own weight (663 MB total), no L2 reuse",
+                       "timing": "CUDA graph of one step, K replays between CUDA events"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "peak_kind": f"HBM copy ({peaks['source']})",
+                         "kernel": "w8a16_skinny_kernel (decode, split-K mma)",
+                         "avg_launch_us": round(avg_launch_us, 3), "traffic": traffic},
+            "e2e": {"value": round(e2e_value, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
+                    "path": "Int8Linear.forward (public API), eager, pinned host x -> device -> y -> pinned host"
+                    if world == 1 else "ColumnParallelInt8Linear.forward, eager, pinned host buffers"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        if prefill:
+            line["prefill"] = prefill
+        if world > 1:
+            line["gemm_only_ms_per_step"] = round(ms_gemm, 5)
+        print(json.dumps(line), flush=True)
+
+    del g_step
+    if g_gemm is not None:
+        del g_gemm
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

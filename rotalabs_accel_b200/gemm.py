@@ -44,7 +44,10 @@ def int8_gemm_torch(x: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Ten
 
 
 def _as_2d_fp16(x: torch.Tensor, K: int) -> torch.Tensor:
-    x2 = x.reshape(-1, K)
+    rows = 1
+    for d in x.shape[:-1]:
+        rows *= d
+    x2 = x.reshape(rows, K)
     if x2.dtype != torch.float16:
         x2 = x2.to(torch.float16)
     if x2.shape[0] > 0 and x2.stride(1) != 1:

@@ -1,0 +1,158 @@
+"""Column-parallel W8A16 layer over several GPUs (one process per GPU).
+
+rotalabs-accel has no distributed code; this is the sharded mode of its
+``Int8Linear`` (src/rotalabs_accel/kernels/gemm.py:241-336).  Output
+channels are split over the ranks: rank r holds rows
+``[r * n_local, (r + 1) * n_local)`` of ``weight_int8`` / ``scale`` (/ ``bias``),
+``n_local = ceil(N / world)`` (the last shard is zero-padded when ``world``
+does not divide ``N``).  Every rank has the whole activation ``x``.
+
+Forward, per rank:
+  1. ``y_local[M, n_local]`` = the sm_100a W8A16 kernel on the local shard;
+  2. one ``all_gather_into_tensor`` of the slices into
+     ``staging[world, M, n_local]`` (NCCL over NVLink on GPUs, gloo on the CPU);
+  3. ``rla_gather_columns`` reorders the staging buffer into ``y[M, N]``
+     (skipped when M == 1: the staging layout already is ``[1, N]``).
+
+Per-channel quantization is row-independent, so quantizing a shard gives
+exactly the rows the full quantization would.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .gemm import int8_gemm
+from .quantization import quantize_weight_per_channel
+
+
+def shard_range(n_total: int, world: int, rank: int):
+    """``(start, stop, n_local)`` of rank's output channels; ``stop - start``
+    may be below ``n_local`` (or 0) for the last ranks when world does not
+    divide ``n_total``."""
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    n_local = -(-n_total // world)
+    start = min(rank * n_local, n_total)
+    stop = min(start + n_local, n_total)
+    return start, stop, n_local
+
+
+def assemble_columns(staging: torch.Tensor, n_total: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``staging[world, M, n_local]`` -> ``[M, n_total]`` (CUDA: the library's
+    gather kernel; CPU: a torch permute)."""
+    world, M, n_local = staging.shape
+    if staging.is_cuda:
+        from . import _capi
+        if n_total == world * n_local:
+            if out is None:
+                out = torch.empty((M, n_total), dtype=staging.dtype, device=staging.device)
+            if M == 1:
+                out.copy_(staging.view(1, n_total))
+                return out
+            return _capi.gather_columns(staging, world, M, n_local, out)
+        full = torch.empty((M, world * n_local), dtype=staging.dtype, device=staging.device)
+        _capi.gather_columns(staging, world, M, n_local, full)
+        y = full[:, :n_total]
+        if out is None:
+            return y.contiguous()
+        out.copy_(y)
+        return out
+    y = staging.permute(1, 0, 2).reshape(M, world * n_local)[:, :n_total]
+    if out is None:
+        return y.contiguous()
+    out.copy_(y)
+    return out
+
+
+class ColumnParallelInt8Linear(torch.nn.Module):
+    """``Int8Linear`` with its output channels split over a process group.
+
+    Buffers (local shard): ``weight_int8`` int8 ``[n_local, in]``, ``scale``
+    fp32 ``[n_local]``, optional fp16 ``bias`` ``[n_local]``.  ``forward``
+    returns the full ``(..., out_features)`` output on every rank.
+    """
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False,
+                 group: Optional[dist.ProcessGroup] = None):
+        super().__init__()
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.in_features = in_features
+        self.out_features = out_features
+        self.start, self.stop, self.n_local = shard_range(out_features, self.world, self.rank)
+        self.register_buffer("weight_int8", torch.zeros(self.n_local, in_features, dtype=torch.int8))
+        self.register_buffer("scale", torch.ones(self.n_local, dtype=torch.float32))
+        if bias:
+            self.bias = torch.nn.Parameter(torch.zeros(self.n_local, dtype=torch.float16))
+        else:
+            self.register_parameter("bias", None)
+        self._quantized = False
+        self._staging = None
+
+    def _check_agreement(self) -> None:
+        """Every rank must shard the same layer: compare (in, out, world) over
+        the group; a mismatch raises on every rank instead of corrupting the
+        gather."""
+        if self.world == 1:
+            return
+        dev = self.weight_int8.device
+        mine = torch.tensor([self.in_features, self.out_features, self.world], dtype=torch.int64,
+                            device=dev if dev.type == "cuda" else "cpu")
+        allv = [torch.zeros_like(mine) for _ in range(self.world)]
+        dist.all_gather(allv, mine, group=self.group)
+        for r, v in enumerate(allv):
+            if not torch.equal(v, mine):
+                raise RuntimeError(f"ColumnParallelInt8Linear: rank {r} has shape {v.tolist()}, "
+                                   f"rank {self.rank} has {mine.tolist()}")
+
+    def quantize_weights(self, weight: torch.Tensor) -> None:
+        """Quantize this rank's rows of the full ``[out, in]`` weight."""
+        assert weight.shape == (self.out_features, self.in_features)
+        self._check_agreement()
+        q, s = quantize_weight_per_channel(weight[self.start:self.stop])
+        self.weight_int8.zero_()
+        self.scale.fill_(1.0)
+        rows = self.stop - self.start
+        self.weight_int8[:rows].copy_(q.to(self.weight_int8.device))
+        self.scale[:rows].copy_(s.to(self.scale.device))
+        self._quantized = True
+
+    def load_shard(self, weight_int8: torch.Tensor, scale: torch.Tensor, bias: Optional[torch.Tensor] = None):
+        """Install an already-quantized full layer's rows for this rank."""
+        assert weight_int8.shape == (self.out_features, self.in_features)
+        self._check_agreement()
+        rows = self.stop - self.start
+        self.weight_int8.zero_()
+        self.scale.fill_(1.0)
+        self.weight_int8[:rows].copy_(weight_int8[self.start:self.stop])
+        self.scale[:rows].copy_(scale[self.start:self.stop].float())
+        if bias is not None and self.bias is not None:
+            self.bias.data.zero_()
+            self.bias.data[:rows].copy_(bias[self.start:self.stop])
+        self._quantized = True
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not self._quantized:
+            raise RuntimeError("Weights not quantized. Call quantize_weights() first.")
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.in_features)
+        M = x2.shape[0]
+        y_local = int8_gemm(x2, self.weight_int8, self.scale, self.bias)
+        if self.world == 1:
+            return y_local[:, :self.out_features].reshape(*lead, self.out_features)
+        staging = torch.empty((self.world, M, self.n_local), dtype=y_local.dtype, device=y_local.device)
+        if y_local.is_cuda:
+            dist.all_gather_into_tensor(staging, y_local.contiguous(), group=self.group)
+        else:
+            dist.all_gather(list(staging.unbind(0)), y_local.contiguous(), group=self.group)
+        y = assemble_columns(staging, self.out_features)
+        return y.reshape(*lead, self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, world={self.world}, "
+                f"rank={self.rank}, rows=[{self.start}, {self.stop}), quantized={self._quantized}")

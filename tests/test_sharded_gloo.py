@@ -1,0 +1,156 @@
+"""Column-parallel sharding on CPU ranks (gloo, world size 2 and 3).
+
+Covers the host-side logic of ``rotalabs_accel_b200.sharded``: the shard
+ranges, the all-gather and the column reassembly give the unsharded
+result; ranks that disagree on the layer shape fail on every rank; a rank
+that never joins the collective makes the others fail with a timeout
+instead of hanging.  The failures are made on the host (a rank raising or
+exiting); nothing here touches a GPU.
+"""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port, timeout_s=60):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _worker_parity(rank, world, port, N, K, M, bias, q):
+    try:
+        _init(rank, world, port)
+        from rotalabs_accel_b200 import int8_gemm_torch, quantize_weight_per_channel
+        from rotalabs_accel_b200.sharded import ColumnParallelInt8Linear
+        g = torch.Generator().manual_seed(7)
+        W = torch.randn(N, K, generator=g) * 0.02
+        b = (torch.randn(N, generator=g) * 0.1).half() if bias else None
+        x = torch.randn(M, K, generator=g).half()
+        m = ColumnParallelInt8Linear(K, N, bias=bias)
+        m.quantize_weights(W)
+        if bias:
+            start, stop = m.start, m.stop
+            m.bias.data[: stop - start].copy_(b[start:stop])
+        y = m(x)
+        wq, s = quantize_weight_per_channel(W)
+        ref = int8_gemm_torch(x, wq, s, b)
+        ok = tuple(y.shape) == (M, N) and torch.allclose(y.float(), ref.float(), rtol=2e-3, atol=2e-3)
+        q.put((rank, bool(ok), float((y.float() - ref.float()).abs().max())))
+        dist.destroy_process_group()
+    except Exception as e:  # report, never hang the parent
+        q.put((rank, False, repr(e)))
+
+
+def _run(fn, world, *args, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, *args, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    for _ in range(world):
+        results.append(q.get(timeout=timeout))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return sorted(results, key=lambda r: r[0])
+
+
+@pytest.mark.parametrize("world,N,K,M,bias", [(2, 256, 128, 3, False), (2, 100, 64, 1, True),
+                                              (3, 97, 96, 5, False)])
+def test_column_parallel_matches_unsharded(world, N, K, M, bias):
+    res = _run(_worker_parity, world, N, K, M, bias)
+    assert all(r[1] for r in res), res
+
+
+def test_shard_ranges_cover_exactly():
+    from rotalabs_accel_b200.sharded import shard_range
+    for N in (1, 7, 64, 100, 11008, 28672):
+        for world in (1, 2, 3, 4, 8):
+            covered = []
+            for r in range(world):
+                a, b, nl = shard_range(N, world, r)
+                assert 0 <= b - a <= nl and nl == -(-N // world)
+                covered.extend(range(a, b))
+            assert covered == list(range(N))
+    with pytest.raises(ValueError):
+        shard_range(10, 2, 2)
+
+
+def test_assemble_columns_cpu():
+    from rotalabs_accel_b200.sharded import assemble_columns
+    st = torch.arange(2 * 3 * 4, dtype=torch.float16).view(2, 3, 4)
+    y = assemble_columns(st, 7)
+    assert y.shape == (3, 7)
+    assert torch.equal(y, torch.cat([st[0], st[1]], dim=1)[:, :7])
+
+
+def _worker_mismatch(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from rotalabs_accel_b200.sharded import ColumnParallelInt8Linear
+        K = 64 if rank == 0 else 32          # rank 1 builds a different layer
+        m = ColumnParallelInt8Linear(K, 128)
+        try:
+            m.quantize_weights(torch.randn(128, K))
+            q.put((rank, False, "no error"))
+        except RuntimeError as e:
+            q.put((rank, "rank" in str(e), str(e)))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+def test_shape_disagreement_fails_on_every_rank():
+    res = _run(_worker_mismatch, 2)
+    assert all(r[1] for r in res), res
+
+
+def _worker_dead_peer(rank, world, port, q):
+    """Rank 1 quits between steps (never reaches the collective); rank 0's
+    next collective must end with an error after the short group timeout."""
+    try:
+        _init(rank, world, port, timeout_s=5)
+        from rotalabs_accel_b200.sharded import ColumnParallelInt8Linear
+        m = ColumnParallelInt8Linear(64, 32)
+        m.quantize_weights(torch.randn(32, 64, generator=torch.Generator().manual_seed(0)))
+        y = m(torch.randn(2, 64).half())          # one good step on both ranks
+        assert y.shape == (2, 32)
+        if rank == 1:
+            q.put((rank, True, "left after step 1"))
+            q.close()
+            q.join_thread()                        # flush the report, then
+            os._exit(0)                            # die without a goodbye
+        try:
+            m(torch.randn(2, 64).half())
+            q.put((rank, False, "collective with a dead peer returned"))
+        except Exception as e:                     # timeout / connection reset
+            q.put((rank, True, type(e).__name__))
+        q.close()
+        q.join_thread()
+        os._exit(0)
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+def test_dead_peer_is_detected_not_hung():
+    res = _run(_worker_dead_peer, 2, timeout=90)
+    assert all(r[1] for r in res), res
