@@ -197,6 +197,42 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def run_case(case: str) -> int:
+    """Small fixed workloads for profiler captures (no timing):
+    ``sweep`` the 16 decode GEMMs once each; ``decode`` 4 launches of
+    M=1, K=4096, N=14336; ``prefill`` 2 launches of M=2048, K=4096, N=11008."""
+    import torch
+    import rotalabs_accel_b200 as ra
+    from rotalabs_accel_b200 import _capi
+    dev = torch.device("cuda", 0)
+
+    def prob(M, N, K, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        x = torch.randn(M, K, generator=g, device=dev).half()
+        q, s = ra.quantize_weight_per_channel(torch.randn(N, K, generator=g, device=dev) * 0.02)
+        return x, q, s.half()
+
+    if case == "sweep":
+        ps = [prob(M, N, K, i) for i, (M, K, N) in enumerate(sweep())]
+        torch.cuda.synchronize()
+        for (x, q, s) in ps:
+            _capi.w8a16_gemm(x, q, s, None)
+    elif case == "decode":
+        x, q, s = prob(1, 14336, 4096, 0)
+        for _ in range(4):
+            _capi.w8a16_gemm(x, q, s, None)
+    elif case == "prefill":
+        x, q, s = prob(2048, 11008, 4096, 0)
+        for _ in range(2):
+            _capi.w8a16_gemm(x, q, s, None)
+    else:
+        raise SystemExit(f"unknown case {case}")
+    torch.cuda.synchronize()
+    err = _capi.device_error()
+    print("case", case, "device_error", err)
+    return 0 if err == 0 else 1
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -206,7 +242,11 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--case", choices=("sweep", "decode", "prefill"),
+                    help="run one small fixed workload for a profiler capture and exit")
     args = ap.parse_args()
+    if args.case:
+        return run_case(args.case)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
