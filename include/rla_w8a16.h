@@ -131,6 +131,27 @@ RLA_API int rla_quantize_per_channel(const void* w, int w_dtype, int64_t ldw, in
 RLA_API int rla_gather_columns(const void* staging, int64_t world, int64_t M, int64_t n_local, void* y, int64_t ldy,
                        void* stream);
 
+/*
+ * Allocation-free W8A16 GEMM for the decode regime.  No counterpart in
+ * rotalabs-accel: it exists for callers that cannot allocate GPU memory
+ * where the GEMM runs -- a serving loop that must not let cudaMalloc
+ * synchronise the device between decode steps, a process whose memory is
+ * reserved up front (KV cache, custom pool), or a plugin/enqueue callback
+ * that gets no workspace.  Same arguments and result as rla_w8a16_gemm
+ * without the workspace: the split-K scratch is a file-scope device array of
+ * 1 MiB per GPU (held by every GPU that loads the library until exit).
+ * Limits: 1 <= M <= 32, K % 16 == 0, 16-byte aligned x and w, ldx % 8 == 0,
+ * ldw % 16 == 0 (else RLA_ERR_UNSUPPORTED); a shape whose split-K plan needs
+ * more than 1 MiB is rejected with RLA_ERR_WORKSPACE.  Nothing is launched
+ * on an error.  The first call on a device sets that device up (looks up the
+ * array's address, zeroes its counters on `stream`): make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * race and must be ordered by the caller.  Never calls cudaMalloc/cudaFree.
+ */
+RLA_API int rla_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
+                                   int scale_dtype, const void* bias, int bias_dtype, void* y, int64_t ldy,
+                                   int64_t M, int64_t N, int64_t K, void* stream);
+
 /* Number of kernels this library has launched in this process (all devices). */
 RLA_API uint64_t rla_launch_count(void);
 

@@ -4,3 +4,4 @@
 #include "rla_skinny.cu"
 #include "rla_tc.cu"
 #include "rla_capi.cu"
+#include "rla_noalloc.cu"

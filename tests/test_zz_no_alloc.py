@@ -1,0 +1,104 @@
+"""The allocation-free decode entry point, ``rla_w8a16_gemm_noalloc``.
+
+It serves callers that cannot allocate GPU memory where the GEMM runs (a
+serving loop that must not let cudaMalloc synchronise the device, a process
+whose memory is reserved up front, a plugin callback that gets no
+workspace): its split-K scratch is a static 1 MiB device array instead of a
+caller workspace.  This test calls it through the C ABI and checks its output
+against ``rla_w8a16_gemm`` (the workspace entry point) on two calls in a row,
+within the tolerance the other GPU tests use, and checks that a shape whose
+scratch need exceeds the array is refused without a launch.
+
+The file is named so that pytest collects it last; it also passes alone in a
+fresh process.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+F16, F32, NONE = 1, 2, 0
+
+
+def _lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from rotalabs_accel_b200 import _capi, build
+    build.build()
+    lib = _capi.load_library()
+    i64, p = ctypes.c_int64, ctypes.c_void_p
+    f = lib.rla_w8a16_gemm_noalloc
+    f.argtypes = [p, i64, p, i64, p, ctypes.c_int, p, ctypes.c_int, p, i64, i64, i64, i64, p]
+    f.restype = ctypes.c_int
+    return lib
+
+
+def _problem(M, N, K, seed, dev):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(M, K, generator=g, device=dev).half()
+    from rotalabs_accel_b200 import quantize_weight_per_channel
+    q, s = quantize_weight_per_channel(torch.randn(N, K, generator=g, device=dev) * 0.02)
+    b = (torch.randn(N, generator=g, device=dev) * 0.1).half()
+    return x, q, s.half(), b
+
+
+def _with_workspace(lib, x, q, s, b, stream):
+    M, K = x.shape
+    N = q.shape[0]
+    y = torch.empty(M, N, dtype=torch.float16, device=x.device)
+    need = lib.rla_w8a16_workspace_size(M, N, K)
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=x.device)
+    st = lib.rla_w8a16_gemm(x.data_ptr(), K, q.data_ptr(), K, s.data_ptr(), F16, b.data_ptr(), F16,
+                            y.data_ptr(), N, M, N, K, ws.data_ptr(), ws.numel(), stream)
+    assert st == 0, lib.rla_last_error()
+    return y
+
+
+def _no_alloc(lib, x, q, s, b, stream):
+    M, K = x.shape
+    N = q.shape[0]
+    y = torch.full((M, N), float("nan"), dtype=torch.float16, device=x.device)
+    st = lib.rla_w8a16_gemm_noalloc(x.data_ptr(), K, q.data_ptr(), K, s.data_ptr(), F16, b.data_ptr(), F16,
+                                    y.data_ptr(), N, M, N, K, stream)
+    assert st == 0, lib.rla_last_error()
+    return y
+
+
+def test_no_alloc_matches_workspace_entry_point():
+    lib = _lib()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    # split-K plans of several shapes (the scratch is really used) and one
+    # without split-K
+    for i, (M, N, K) in enumerate([(8, 1024, 28672), (16, 4096, 4096), (1, 512, 8192), (4, 14336, 4096)]):
+        x, q, s, b = _problem(M, N, K, 100 + i, dev)
+        y_ws = _with_workspace(lib, x, q, s, b, stream)
+        ref = x.float() @ (q.float() * s.float()[:, None]).t() + b.float()
+        for _ in range(2):                              # two calls in a row share the array
+            y = _no_alloc(lib, x, q, s, b, stream)
+            torch.cuda.synchronize()
+            assert torch.isfinite(y).all()
+            assert (y.float() - y_ws.float()).abs().max().item() <= TOL
+            assert (y.float() - ref).abs().max().item() <= TOL + 2.0 ** -10 * ref.abs().max().item()
+
+
+def test_no_alloc_rejects_oversized_scratch():
+    lib = _lib()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    M, N, K = 32, 4096, 4096            # split-K plan needs 1 MiB + 4 KiB > the 1 MiB array
+    x, q, s, b = _problem(M, N, K, 7, dev)
+    y = torch.zeros(M, N, dtype=torch.float16, device=dev)
+    torch.cuda.synchronize()
+    n0 = lib.rla_launch_count()
+    st = lib.rla_w8a16_gemm_noalloc(x.data_ptr(), K, q.data_ptr(), K, s.data_ptr(), F16, None, NONE,
+                                    y.data_ptr(), N, M, N, K, stream)
+    assert st == 4                      # RLA_ERR_WORKSPACE
+    assert b"static scratch" in lib.rla_last_error()
+    assert lib.rla_launch_count() == n0
+    torch.cuda.synchronize()
+    assert (y == 0).all()
