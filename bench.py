@@ -200,7 +200,8 @@ def run_reference(args):
 def run_case(case: str) -> int:
     """Small fixed workloads for profiler captures (no timing):
     ``sweep`` the 16 decode GEMMs once each; ``decode`` 4 launches of
-    M=1, K=4096, N=14336; ``prefill`` 2 launches of M=2048, K=4096, N=11008."""
+    M=1, K=4096, N=14336; ``decode-large`` 3 launches of M=1, K=8192,
+    N=28672; ``prefill`` 2 launches of M=2048, K=4096, N=11008."""
     import torch
     import rotalabs_accel_b200 as ra
     from rotalabs_accel_b200 import _capi
@@ -220,6 +221,10 @@ def run_case(case: str) -> int:
     elif case == "decode":
         x, q, s = prob(1, 14336, 4096, 0)
         for _ in range(4):
+            _capi.w8a16_gemm(x, q, s, None)
+    elif case == "decode-large":
+        x, q, s = prob(1, 28672, 8192, 0)
+        for _ in range(3):
             _capi.w8a16_gemm(x, q, s, None)
     elif case == "prefill":
         x, q, s = prob(2048, 11008, 4096, 0)
@@ -242,7 +247,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--case", choices=("sweep", "decode", "prefill"),
+    ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "prefill"),
                     help="run one small fixed workload for a profiler capture and exit")
     args = ap.parse_args()
     if args.case:
@@ -466,7 +471,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_kind": f"HBM copy ({peaks['source']})",
-                         "kernel": "w8a16_skinny_kernel (decode, split-K mma)",
+                         "kernel": "decode kernels: w8a16_skinny_kernel (split-K, small layers) and "
+                                   "w8a16_stream_kernel (persistent stream-K TMA, large layers), per the selector",
                          "avg_launch_us": round(avg_launch_us, 3), "traffic": traffic},
             "e2e": {"value": round(e2e_value, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),

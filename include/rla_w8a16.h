@@ -53,8 +53,19 @@ typedef enum rla_kernel {
   RLA_KERNEL_SKINNY = 1,   /* HBM-streaming split-K kernel, M <= 32 (decode)     */
   RLA_KERNEL_TCGEN05 = 2,  /* TMA + int8->fp16 into TMEM + tcgen05.mma (prefill) */
   RLA_KERNEL_GENERIC = 3,  /* any alignment / any K (ragged shapes)              */
-  RLA_KERNEL_FILL = 4      /* K == 0: y = bias (or 0)                            */
+  RLA_KERNEL_FILL = 4,     /* K == 0: y = bias (or 0)                            */
+  RLA_KERNEL_STREAM = 5    /* persistent stream-K TMA decode kernel, M <= 32     */
 } rla_kernel;
+
+/*
+ * Process-wide choice of the decode (M <= 32) kernel family:
+ * RLA_KERNEL_NONE (0, the default) lets the selector choose; RLA_KERNEL_SKINNY
+ * or RLA_KERNEL_STREAM force that kernel where it applies.  For A/B
+ * measurements and tests; not synchronised with GEMM calls running
+ * concurrently on other threads.  Part of the per-shape selector that
+ * replaces the Triton autotuner (src/rotalabs_accel/kernels/gemm.py:53-65).
+ */
+RLA_API int rla_set_decode_kernel(int kernel);
 
 /*
  * W8A16 GEMM on device buffers.
@@ -70,8 +81,8 @@ typedef enum rla_kernel {
  *   scale  [N], scale_dtype RLA_DTYPE_F32 (Int8Linear) or RLA_DTYPE_F16
  *   bias   [N] or NULL; bias_dtype RLA_DTYPE_NONE / F16 / F32
  *   y      fp16 [M, N], row stride ldy elements (ldy >= N)
- *   workspace / workspace_bytes: caller-owned device scratch for split-K
- *          partial sums, at least rla_w8a16_workspace_size(M, N, K) bytes,
+ *   workspace / workspace_bytes: caller-owned device scratch for split-K /
+ *          stream-K partial sums, at least rla_w8a16_workspace_size(M, N, K) bytes,
  *          256-byte aligned.  Layout: the first 4096 bytes hold arrival
  *          counters that must be zero before the first call (the library
  *          leaves them at zero after every call, so one workspace serves

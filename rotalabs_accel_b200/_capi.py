@@ -20,11 +20,13 @@ LIB_PATH = os.path.join(_HERE, "librla_w8a16.so")
 
 RLA_OK = 0
 DTYPE_NONE, DTYPE_F16, DTYPE_F32, DTYPE_BF16 = 0, 1, 2, 3
-KERNEL_NAMES = {0: "none", 1: "skinny", 2: "tcgen05", 3: "generic", 4: "fill"}
+KERNEL_NAMES = {0: "none", 1: "skinny", 2: "tcgen05", 3: "generic", 4: "fill", 5: "stream"}
+KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 
 EXPORTED_SYMBOLS = (
     "rla_w8a16_gemm", "rla_w8a16_workspace_size", "rla_w8a16_plan", "rla_quantize_per_channel",
     "rla_gather_columns", "rla_launch_count", "rla_get_device_error", "rla_last_error", "rla_version",
+    "rla_set_decode_kernel",
 )
 
 _lib = None
@@ -68,6 +70,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.rla_last_error.restype = ctypes.c_char_p
         lib.rla_version.argtypes = []
         lib.rla_version.restype = ctypes.c_int
+        lib.rla_set_decode_kernel.argtypes = [ctypes.c_int]
+        lib.rla_set_decode_kernel.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -176,6 +180,13 @@ def gather_columns(staging: torch.Tensor, world: int, M: int, n_local: int, out:
         st = lib.rla_gather_columns(staging.data_ptr(), world, M, n_local, out.data_ptr(), out.stride(0), stream)
     _check(st, "rla_gather_columns")
     return out
+
+
+def set_decode_kernel(name: str) -> None:
+    """Force the decode (M <= 32) kernel family process-wide: "auto" (the
+    selector's choice), "skinny" or "stream".  For A/B runs and tests."""
+    kid = 0 if name == "auto" else KERNEL_IDS[name]
+    _check(load_library().rla_set_decode_kernel(kid), "rla_set_decode_kernel")
 
 
 def launch_count() -> int:

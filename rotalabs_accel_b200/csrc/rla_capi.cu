@@ -76,6 +76,23 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   if (p.splits > 1) p.workspace = kSplitCounterBytes + (size_t)p.splits * (size_t)M * (size_t)N * 4;
 }
 
+static std::atomic<int> g_decode_kernel{RLA_KERNEL_NONE};
+
+// Persistent stream-K decode kernel: one CTA per SM (fewer if the problem has
+// fewer 128-row x 128-k units), each streaming an equal share of the weight
+// bytes.  Needs the workspace for the pieces of row blocks split between CTAs.
+static void stream_shape(Plan& p, int64_t M, int64_t N, int64_t K, int sms) {
+  p.kernel = RLA_KERNEL_STREAM;
+  p.nt = M <= 8 ? 1 : M <= 16 ? 2 : 4;
+  const int64_t units = ((N + 127) / 128) * ((K + 127) / 128);
+  p.grid_x = static_cast<int>(units < sms ? units : sms);
+  p.grid_y = 1;
+  p.splits = 1;
+  p.threads = 288;
+  p.smem = stream_smem_bytes(p.nt);
+  p.workspace = stream_workspace_bytes(M, p.grid_x);
+}
+
 Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace) {
   Plan p;
   if (M == 0 || N == 0) return p;
@@ -85,6 +102,19 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
   }
   const int sms = device_sm_count();
   if (aligned && K % 16 == 0 && M <= 32) {
+    const int choice = g_decode_kernel.load(std::memory_order_relaxed);
+    // Measured on B200 (CUDA graphs of back-to-back launches): the persistent
+    // stream-K kernel wins on large weights, and from M = 9 on weights of
+    // 40 MB or more; the skinny kernel wins on smaller layers and on narrow
+    // column shards (lower fixed cost per launch).
+    const double wbytes = static_cast<double>(N) * static_cast<double>(K);
+    const bool stream_wins = M <= 16 && ((M > 8 && wbytes >= 40e6) || wbytes >= 120e6);
+    const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
+    // The stream kernel keeps one arrival counter per CTA in the counter region.
+    if (have_workspace && want_stream && sms <= kMaxSplitRowBlocks) {
+      stream_shape(p, M, N, K, sms);
+      return p;
+    }
     skinny_shape(p, M, N, K, have_workspace, sms);
     return p;
   }
@@ -123,6 +153,13 @@ extern "C" {
 
 int rla_version(void) { return 1 * 10000 + 0 * 100 + 0; }
 
+int rla_set_decode_kernel(int kernel) {
+  if (kernel != RLA_KERNEL_NONE && kernel != RLA_KERNEL_SKINNY && kernel != RLA_KERNEL_STREAM)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_set_decode_kernel: expected NONE, SKINNY or STREAM");
+  g_decode_kernel.store(kernel, std::memory_order_relaxed);
+  return RLA_OK;
+}
+
 const char* rla_last_error(void) { return g_err; }
 
 uint64_t rla_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
@@ -155,8 +192,9 @@ int rla_w8a16_plan(int64_t M, int64_t N, int64_t K, int aligned, int have_worksp
     params[2] = p.grid_y;
     params[3] = p.threads;
     params[4] = p.splits;
-    params[5] = p.kernel == RLA_KERNEL_SKINNY ? 16 * p.wn : p.kernel == RLA_KERNEL_TCGEN05 ? 128 : 0;
-    params[6] = p.kernel == RLA_KERNEL_SKINNY ? 8 * p.nt : p.bm;
+    params[5] = p.kernel == RLA_KERNEL_SKINNY ? 16 * p.wn
+                : (p.kernel == RLA_KERNEL_STREAM || p.kernel == RLA_KERNEL_TCGEN05) ? 128 : 0;
+    params[6] = (p.kernel == RLA_KERNEL_SKINNY || p.kernel == RLA_KERNEL_STREAM) ? 8 * p.nt : p.bm;
     params[7] = static_cast<int64_t>(p.smem);
   }
   return RLA_OK;
@@ -192,6 +230,7 @@ int rla_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, con
   cudaError_t e = cudaSuccess;
   switch (p.kernel) {
     case RLA_KERNEL_SKINNY: e = launch_skinny(a, p, workspace, s); break;
+    case RLA_KERNEL_STREAM: e = launch_stream(a, p, workspace, s); break;
     case RLA_KERNEL_TCGEN05: e = launch_tcgen05(a, p, s); break;
     case RLA_KERNEL_GENERIC: e = launch_generic(a, s); break;
     case RLA_KERNEL_FILL: e = launch_fill(a, s); break;

@@ -94,6 +94,19 @@ RLA_DEVFN void rla_mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start before its predecessor in the stream has finished;
+// griddepcontrol.wait blocks until the predecessor has completed and its
+// memory is visible, so every read of data a predecessor may write comes
+// after it.  launch_dependents lets the next such kernel start launching.
+// Both are no-ops for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+RLA_DEVFN void rla_griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+RLA_DEVFN void rla_griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Pull the cache line holding `p` into L2 (never stale: L2 is coherent).
+RLA_DEVFN void rla_prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+// ---------------------------------------------------------------------------
 // Shared memory / mbarrier
 // ---------------------------------------------------------------------------
 RLA_DEVFN uint32_t rla_smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -128,6 +141,19 @@ RLA_DEVFN bool rla_mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same, but the thread may be suspended in hardware for up to `hint_ns`
+// while the phase is incomplete (no issue slots spent polling).
+RLA_DEVFN bool rla_mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(rla_smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false (after recording `err`) if it did not complete within the limit or
 // if *abort_flag was raised by another warp of this CTA.
@@ -136,8 +162,8 @@ RLA_DEVFN bool rla_mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err, v
   const uint64_t t0 = rla_globaltimer();
   uint32_t spins = 0;
   while (true) {
-    if (rla_mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0) {
+    if (rla_mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+    if ((++spins & 15u) == 0) {
       if (abort_flag && *abort_flag) return false;
       if (rla_globaltimer() - t0 > RLA_WAIT_LIMIT_NS) {
         rla_record_error(err);

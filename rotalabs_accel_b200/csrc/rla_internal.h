@@ -53,6 +53,9 @@ void note_launch();
 void set_error(const char* fmt, ...);
 
 cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
+cudaError_t launch_stream(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
+size_t stream_workspace_bytes(int64_t M, int ctas);
+size_t stream_smem_bytes(int nt);
 cudaError_t launch_tcgen05(const GemmArgs& a, const Plan& p, cudaStream_t s);
 cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s);
 cudaError_t launch_fill(const GemmArgs& a, cudaStream_t s);

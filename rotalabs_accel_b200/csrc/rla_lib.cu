@@ -2,6 +2,7 @@
 // needed for the shared device-side error word).
 #include "rla_misc.cu"
 #include "rla_skinny.cu"
+#include "rla_stream.cu"
 #include "rla_tc.cu"
 #include "rla_capi.cu"
 #include "rla_noalloc.cu"

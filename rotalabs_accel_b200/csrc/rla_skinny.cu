@@ -21,6 +21,10 @@
 //   MMA step s (0..3), fragment k columns {2q, 2q+1} <- k = kb+16q+4s+{0,1}
 //                                         {2q+8, 2q+9} <- k = kb+16q+4s+{2,3}
 // int8 -> fp16 happens in registers (rla_i8x4_to_h2x2).
+//
+// Launched with programmatic dependent launch: a CTA warms L2 with its first
+// weight bytes while the previous kernel in the stream finishes, and reads
+// nothing before that kernel is done (rla_griddep_wait).
 #include "rla_common.cuh"
 #include "rla_internal.h"
 
@@ -68,6 +72,19 @@ __global__ void __launch_bounds__(32 * WN * WK)
   float acc[NT][4];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+
+  // Let the next launch in the stream start, warm L2 with this lane's first
+  // batch of weight bytes, then wait for the predecessor before any real read.
+  rla_griddep_launch_dependents();
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int cc = c_begin + wk + u * WK;
+    if (cc < c_end && cc * 64 + q * 16 < K) {
+      rla_prefetch_l2(wrow0 + cc * 64);
+      rla_prefetch_l2(wrow1 + cc * 64);
+    }
+  }
+  rla_griddep_wait();
 
   const uint4 zero4 = make_uint4(0, 0, 0, 0);
   for (int c = c_begin + wk; c < c_end; c += WK * U) {
@@ -206,11 +223,19 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
     counters = static_cast<unsigned int*>(workspace);
     partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kSplitCounterBytes);
   }
-  dim3 grid(p.grid_x, p.splits);
-  w8a16_skinny_kernel<NT, WN, WK, U><<<grid, 32 * WN * WK, 0, s>>>(
-      static_cast<const __half*>(a.x), a.ldx, a.w, a.ldw, a.scale, a.scale_f32, a.bias, a.bias_kind,
-      static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K, cps, partial, counters);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid_x, p.splits);
+  cfg.blockDim = dim3(32 * WN * WK);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see rla_griddep_wait
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, w8a16_skinny_kernel<NT, WN, WK, U>, static_cast<const __half*>(a.x), a.ldx, a.w,
+                            a.ldw, a.scale, a.scale_f32, a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M,
+                            a.N, a.K, cps, partial, counters);
 }
 
 // Instantiated configurations: NT in {1, 2, 4}; (WN, WK) in {(1, 8), (2, 4), (4, 2)}.

@@ -28,13 +28,9 @@
 //
 // All waits are bounded (rla_mbar_wait); a timeout records a device error,
 // raises a CTA-wide abort flag and unwinds to the TMEM release.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
 #include "rla_common.cuh"
 #include "rla_internal.h"
+#include "rla_tmap.cuh"
 
 namespace rla {
 
@@ -228,35 +224,8 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Host side: tensor maps (through the driver entry point, no libcuda link)
+// Host side
 // ---------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-static bool make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-                         uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
-                         CUtensorMapSwizzle swz) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 size_t tcgen05_smem_bytes(int bm, int stages) {
   size_t per_stage = (size_t)bm * 128 + tc::W_TILE_BYTES;
   return per_stage * stages + 1024 /* barriers etc. */ + 1024 /* alignment slack */;

@@ -71,13 +71,16 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
 
 
 def test_selector_rules(lib):
-    # decode regime -> the skinny HBM-streaming kernel
+    # decode regime: the persistent stream-K kernel on large weights (and from
+    # M = 9 on weights >= 40 MB), the skinny kernel otherwise
     for M in (1, 4, 8, 16, 32):
-        for K, N in ((4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336)):
+        for K, N in ((4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336), (8192, 28672), (28672, 1024)):
             p = _capi.plan(M, N, K)
-            assert p["kernel_name"] == "skinny"
+            big = M <= 16 and ((M > 8 and N * K >= 40e6) or N * K >= 120e6)
+            assert p["kernel_name"] == ("stream" if big else "skinny"), (M, N, K)
             assert p["x_rows"] >= M and p["x_rows"] <= 32
-            assert p["grid_x"] * p["w_rows"] >= N
+            if p["kernel_name"] == "skinny":
+                assert p["grid_x"] * p["w_rows"] >= N
     # narrow column shards with long K get split-K across CTAs
     p = _capi.plan(1, 1024, 28672)
     assert p["kernel_name"] == "skinny" and p["splits"] > 1
@@ -88,6 +91,19 @@ def test_selector_rules(lib):
         assert p["kernel_name"] == "tcgen05" and p["w_rows"] == 128
         assert p["grid_x"] * 128 >= N and p["grid_y"] * p["x_rows"] >= 2048
         assert p["smem"] <= 227 * 1024
+    # the persistent stream-K decode kernel, when chosen: at most one CTA per SM
+    _capi.set_decode_kernel("stream")
+    try:
+        for M in (1, 8, 16, 32):
+            p = _capi.plan(M, 14336, 4096)
+            assert p["kernel_name"] == "stream" and p["grid_x"] <= 148 and p["grid_y"] == 1
+            assert p["x_rows"] >= M and p["smem"] <= 227 * 1024
+            assert lib.rla_w8a16_workspace_size(M, 14336, 4096) == 4096 + p["grid_x"] * 2 * 128 * M * 4
+        assert _capi.plan(1, 16, 64)["grid_x"] == 1          # one 128x128 unit -> one CTA
+        assert _capi.plan(1, 1024, 28672, have_workspace=False)["kernel_name"] == "skinny"
+    finally:
+        _capi.set_decode_kernel("auto")
+    assert lib.rla_set_decode_kernel(2) == 1                 # only NONE / SKINNY / STREAM
     # unaligned / ragged -> generic; K == 0 -> fill; empty -> none
     assert _capi.plan(4, 64, 64, aligned=False)["kernel_name"] == "generic"
     assert _capi.plan(4, 64, 40)["kernel_name"] == "generic"        # K % 16 != 0 on the skinny path

@@ -107,16 +107,42 @@ def test_config0_vs_golden(dev, golden_dir):
     assert (y.float() - gold).abs().max().item() <= 2 * TOL
 
 
+@pytest.fixture(params=["stream", "skinny"])
+def decode_kernel(request, dev):
+    """Run a decode test once per decode kernel family."""
+    from rotalabs_accel_b200 import _capi
+    _capi.set_decode_kernel(request.param)
+    yield request.param
+    _capi.set_decode_kernel("auto")
+
+
 @pytest.mark.parametrize("M", [1, 4, 8, 16])
 @pytest.mark.parametrize("KN", [(4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336)])
-def test_decode_sweep(dev, M, KN):
+def test_decode_sweep(dev, decode_kernel, M, KN):
     """the decode GEMV sweep at full size."""
     from rotalabs_accel_b200 import int8_gemm, _capi
     K, N = KN
     x, q, s = _problem(M, N, K, seed=M * 7 + K + N)
-    assert _capi.plan(M, N, K)["kernel_name"] == "skinny"
+    assert _capi.plan(M, N, K)["kernel_name"] == decode_kernel
     y = int8_gemm(x, q, s)
     _check(y, _fp32_ref(x, q, s))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 16), (3, 33, 64), (7, 129, 80), (17, 100, 272), (31, 257, 1024),
+                                   (32, 4096, 4096), (8, 1024, 28672), (16, 64, 65536), (2, 5000, 48),
+                                   (9, 192, 4160), (1, 7, 4096)])
+@pytest.mark.parametrize("bias", [None, "f16"])
+def test_decode_kernels_ragged(dev, decode_kernel, M, N, K, bias):
+    """Ragged decode shapes on both decode kernels: partial row blocks, K not a
+    multiple of the stage, row blocks split across many CTAs."""
+    from rotalabs_accel_b200 import int8_gemm, _capi
+    x, q, s = _problem(M, N, K, seed=M * 31 + N + K)
+    b = (torch.randn(N, device=dev) * 0.1).half() if bias else None
+    assert _capi.plan(M, N, K)["kernel_name"] == decode_kernel
+    y1 = int8_gemm(x, q, s, b)
+    y2 = int8_gemm(x, q, s, b)
+    assert torch.equal(y1, y2)          # fixed-order reductions: bit-reproducible
+    _check(y1, _fp32_ref(x, q, s, b))
 
 
 @pytest.mark.parametrize("KN", [(4096, 12288), (4096, 11008), (11008, 4096)])
@@ -226,12 +252,18 @@ def test_workspace_shared_across_shapes(dev):
     counter region must not overlap an earlier call's partial sums."""
     from rotalabs_accel_b200 import int8_gemm, _capi
     shapes = [(4, 256, 1024), (16, 4096, 4096), (1, 1024, 28672), (16, 256, 4096), (8, 512, 8192),
-              (16, 4096, 4096)]
+              (16, 4096, 4096), (32, 4096, 4096)]
     probs = [_problem(M, N, K, seed=i) for i, (M, N, K) in enumerate(shapes)]
-    for _ in range(2):
-        for (M, N, K), (x, q, s) in zip(shapes, probs):
-            assert _capi.plan(M, N, K)["splits"] > 1
-            _check(int8_gemm(x, q, s), _fp32_ref(x, q, s))
+    # the two decode kernels use the same workspace with the same fixed layout
+    for kern in ("skinny", "stream", "skinny", "stream"):
+        _capi.set_decode_kernel(kern)
+        try:
+            for (M, N, K), (x, q, s) in zip(shapes, probs):
+                if kern == "skinny":
+                    assert _capi.plan(M, N, K)["splits"] > 1
+                _check(int8_gemm(x, q, s), _fp32_ref(x, q, s))
+        finally:
+            _capi.set_decode_kernel("auto")
 
 
 def test_fp32_and_bf16_activations(dev):
