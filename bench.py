@@ -68,8 +68,8 @@ def load_peaks():
 
 def load_traffic():
     """Per-launch DRAM bytes of the decode kernel over the sweep, from the
-    committed ncu summary (profiles/skinny_decode_sweep.md)."""
-    p = os.path.join(ROOT, "profiles", "skinny_decode_sweep.md")
+    committed ncu summary (profiles/decode_sweep_traffic.md)."""
+    p = os.path.join(ROOT, "profiles", "decode_sweep_traffic.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
