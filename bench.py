@@ -6,8 +6,11 @@ M in {1, 4, 8, 16} x (K, N) in {(4096, 4096), (4096, 11008), (11008, 4096),
 weights in all, > the 126 MB L2, so every GEMM streams its weight from HBM).
 x ~ N(0, 1) fp16, W ~ N(0, 0.02) quantized per output channel, fp16 scales,
 seeded synthetic data.  With N GPUs every layer is column-parallel: each
-rank holds N_layer / world output channels, runs its slice and the slices
-are all-gathered over NCCL and reassembled (strong scaling).
+rank holds N_layer / world output channels and runs its slice; by default
+(``--exchange p2p``) the decode kernel sends its slice to every peer over
+NVLink as flagged words and unpacks theirs in the same launch
+(``rla_w8a16_gemm_allgather``); ``--exchange nccl`` all-gathers the slices
+with NCCL and reassembles them instead (strong scaling either way).
 
 Reported (rank 0, one line):
   value      algorithmic bytes of the whole sweep (sum of N*K + 2MK + 2N + 2MN
@@ -247,6 +250,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
+                    help="N > 1: output exchange of the column-parallel layers")
     ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "prefill"),
                     help="run one small fixed workload for a profiler capture and exit")
     args = ap.parse_args()
@@ -274,6 +279,7 @@ def main():
 
     import rotalabs_accel_b200 as ra
     from rotalabs_accel_b200 import _capi
+    from rotalabs_accel_b200.peer import PeerExchange
     from rotalabs_accel_b200.sharded import ColumnParallelInt8Linear, assemble_columns, shard_range
 
     peaks = load_peaks()
@@ -291,10 +297,13 @@ def main():
         s = s.half()
         y_local = torch.empty(M, n_local, device=dev, dtype=torch.float16)
         staging = torch.empty(world, M, n_local, device=dev, dtype=torch.float16) if world > 1 else None
-        y = torch.empty(M, N, device=dev, dtype=torch.float16)
+        y = torch.empty(M, world * n_local, device=dev, dtype=torch.float16)
         layers.append(dict(M=M, K=K, N=N, x=x, q=q, s=s, y_local=y_local, staging=staging, y=y, n_local=n_local))
     torch.cuda.synchronize()
     bytes_step = sum(gemm_bytes(M, K, N) for (M, K, N) in jobs)
+    p2p = world > 1 and args.exchange == "p2p"
+    exchange = PeerExchange(max_rows=max(L["M"] for L in layers),
+                            max_n_local=max(L["n_local"] for L in layers)) if p2p else None
 
     stream = torch.cuda.Stream(device=dev)
 
@@ -306,6 +315,8 @@ def main():
         for L in layers:
             if world == 1:
                 _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y"])
+            elif p2p:
+                exchange.gemm(L["x"], L["q"], L["s"], None, out=L["y"])
             else:
                 _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y_local"])
                 dist.all_gather_into_tensor(L["staging"], L["y_local"])
@@ -349,9 +360,9 @@ def main():
             ms = t.item()
         return ms, clocks
 
-    launches_per_step = len(layers) * (1 if world == 1 else 2)   # GEMM (+ gather kernel; M=1 uses a copy)
-    if world > 1:
-        launches_per_step = len(layers) + sum(1 for L in layers if L["M"] > 1)
+    launches_per_step = len(layers)   # one GEMM kernel per layer (the fused exchange included)
+    if world > 1 and not p2p:
+        launches_per_step = len(layers) + sum(1 for L in layers if L["M"] > 1)   # + gather kernel (M=1: a copy)
 
     g_step = capture(step)
     ms_step, clocks = timed(g_step, args.steps, args.warmup, sample_clocks=(rank == 0))
@@ -380,6 +391,8 @@ def main():
             m.weight_int8.copy_(L["q"])
             m.scale.copy_(L["s"].float())
             m._quantized = True
+            if p2p:
+                m.enable_peer_exchange(max_tokens=L["M"], exchange=exchange)
         else:
             m = ra.Int8Linear(L["K"], L["N"])
             m.weight_int8 = L["q"]
@@ -464,7 +477,9 @@ def main():
             "config": {"workload": "decode GEMV sweep, BASELINE config 1: M in {1,4,8,16} x (K,N) in "
                                    "{(4096,4096),(4096,11008),(11008,4096),(4096,14336)}, 16 GEMMs per step",
                        "parallelism": "single GPU" if world == 1 else
-                       f"column-parallel over {world} GPUs + NCCL all-gather of each output",
+                       (f"column-parallel over {world} GPUs, peer-to-peer all-gather fused into the decode kernel "
+                        "(flagged-word stores over NVLink, unpacked in the same launch)" if p2p else
+                        f"column-parallel over {world} GPUs + NCCL all-gather of each output"),
                        "weights_bytes": sum(L["q"].numel() for L in layers) * world,
                        "l2": "working set > L2: each GEMM has its own weight (663 MB total), no L2 reuse",
                        "timing": "CUDA graph of one step, K replays between CUDA events"},
@@ -492,6 +507,8 @@ def main():
     if g_gemm is not None:
         del g_gemm
     torch.cuda.synchronize()
+    if exchange is not None:
+        exchange.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

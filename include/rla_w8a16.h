@@ -163,13 +163,83 @@ RLA_API int rla_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, 
                                    int scale_dtype, const void* bias, int bias_dtype, void* y, int64_t ldy,
                                    int64_t M, int64_t N, int64_t K, void* stream);
 
+/*
+ * Column-parallel W8A16 GEMM with a direct peer-to-peer all-gather epilogue
+ * (one process per GPU on one node).  No counterpart in rotalabs-accel, which
+ * has no distributed code: it is the fused form of the sharded Int8Linear's
+ * "local GEMM + ncclAllGather + reorder" (rank r holds rows
+ * [r * n_local, (r + 1) * n_local) of weight_int8 / scale / bias,
+ * src/rotalabs_accel/kernels/gemm.py:268-279 split by output channel).
+ *
+ * Rank `rank` of `world` (1 <= world <= RLA_MAX_PEERS) computes its slice
+ *     y[m, rank * n_local + j] = fp16( scale[j] * sum_k x[m, k] * w[j, k] (+ bias[j]) ),
+ *     0 <= j < n_local,
+ * into its own y and, as 8-byte flagged words {two fp16 values, call number},
+ * into the receive buffer of every peer over NVLink; the last CTAs of the
+ * launch then unpack every peer's slice from this rank's receive buffer into
+ * y.  When the kernel has completed, y[M, world * n_local] (row stride ldy)
+ * holds all slices: no gather, no reorder, no host synchronisation.
+ *
+ *   x, ldx, w (int8 [n_local, K], row stride ldw), scale, bias, workspace:
+ *          as in rla_w8a16_gemm, with N = n_local.
+ *   y      this rank's fp16 output [M, ldy], ldy >= world * n_local (any
+ *          device memory; not shared with the peers).
+ *   recv_peers  HOST array of `world` device pointers, valid in this process,
+ *          to every rank's receive buffer (recv_peers[rank] is this rank's;
+ *          the peers' mapped with rla_ipc_open), each recv_bytes bytes from
+ *          rla_peer_alloc (zeroed, 16-byte aligned).  Needs
+ *          recv_bytes >= 16 * world * ceil(M / 2) * n_local, else
+ *          RLA_ERR_WORKSPACE.
+ *   sync   this rank's sync area, RLA_PEER_SYNC_BYTES of zeroed device memory
+ *          (128-byte aligned), used by no other exchange.
+ *
+ * Every rank must make the same sequence of calls with the same shapes,
+ * stream-ordered on each rank (as with the collectives of one communicator).
+ * Decode shapes only (1 <= M <= 32, K % 16 == 0, 16-byte aligned x and w,
+ * ldx % 8 == 0, ldw % 16 == 0): otherwise RLA_ERR_UNSUPPORTED with nothing
+ * launched, and the caller uses its collective path.  Waits are bounded
+ * (rla_set_peer_wait_limit); a wait that gives up records device error 7 (a
+ * peer's slice did not arrive) or 8 (this launch's CTAs did not all finish)
+ * and leaves y incomplete; after that, free and re-create the buffers on
+ * every rank.  Stores to peers are plain stores over NVLink (no multicast).
+ */
+#define RLA_MAX_PEERS 8
+#define RLA_PEER_SYNC_BYTES 512
+#define RLA_IPC_HANDLE_BYTES 64
+RLA_API int rla_w8a16_gemm_allgather(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
+                                     int scale_dtype, const void* bias, int bias_dtype, void* y, int64_t ldy,
+                                     int64_t M, int64_t n_local, int64_t K, void* const* recv_peers,
+                                     size_t recv_bytes, void* sync, int rank, int world, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+/* Limit of every wait inside rla_w8a16_gemm_allgather, in nanoseconds
+ * (default 1 s; 1 ms .. 60 s).  Process-wide. */
+RLA_API int rla_set_peer_wait_limit(uint64_t ns);
+
+/*
+ * Device memory for the peer exchange: rla_peer_alloc returns `bytes` of
+ * zeroed device memory on the current device (its own cudaMalloc, so the IPC
+ * handle covers exactly this buffer); rla_peer_free releases it.
+ * rla_ipc_export writes the RLA_IPC_HANDLE_BYTES-byte IPC handle of such a
+ * buffer into `handle` (host memory); another process on the same node opens
+ * it with rla_ipc_open (peer access enabled lazily) and closes it with
+ * rla_ipc_close.  These replace nothing in rotalabs-accel; they are the
+ * set-up of rla_w8a16_gemm_allgather.
+ */
+RLA_API int rla_peer_alloc(size_t bytes, void** ptr);
+RLA_API int rla_peer_free(void* ptr);
+RLA_API int rla_ipc_export(const void* ptr, void* handle);
+RLA_API int rla_ipc_open(const void* handle, void** ptr);
+RLA_API int rla_ipc_close(void* ptr);
+
 /* Number of kernels this library has launched in this process (all devices). */
 RLA_API uint64_t rla_launch_count(void);
 
 /* Reads and clears the device-side error word of the current device (0 = no
  * error; otherwise a bounded wait inside a kernel gave up: 1 TMA tile,
  * 2 free slot, 3 converted operand, 4 operand slot, 5 accumulator,
- * 6 split-K partner).  Synchronises the device. */
+ * 6 split-K partner, 7 a peer's slice of an exchange call did not arrive,
+ * 8 an exchange launch's CTAs did not all finish).  Synchronises the device. */
 RLA_API int rla_get_device_error(unsigned int* code);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */

@@ -26,8 +26,13 @@ KERNEL_IDS = {v: k for k, v in KERNEL_NAMES.items()}
 EXPORTED_SYMBOLS = (
     "rla_w8a16_gemm", "rla_w8a16_workspace_size", "rla_w8a16_plan", "rla_quantize_per_channel",
     "rla_gather_columns", "rla_launch_count", "rla_get_device_error", "rla_last_error", "rla_version",
-    "rla_set_decode_kernel",
+    "rla_set_decode_kernel", "rla_w8a16_gemm_allgather", "rla_set_peer_wait_limit", "rla_peer_alloc",
+    "rla_peer_free", "rla_ipc_export", "rla_ipc_open", "rla_ipc_close",
 )
+
+MAX_PEERS = 8
+PEER_SYNC_BYTES = 512
+IPC_HANDLE_BYTES = 64
 
 _lib = None
 _lib_lock = threading.Lock()
@@ -72,6 +77,22 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.rla_version.restype = ctypes.c_int
         lib.rla_set_decode_kernel.argtypes = [ctypes.c_int]
         lib.rla_set_decode_kernel.restype = ctypes.c_int
+        pp = ctypes.POINTER(p)
+        lib.rla_w8a16_gemm_allgather.argtypes = [p, i64, p, i64, p, ctypes.c_int, p, ctypes.c_int, p, i64, i64,
+                                                 i64, i64, pp, sz, p, ctypes.c_int, ctypes.c_int, p, sz, p]
+        lib.rla_w8a16_gemm_allgather.restype = ctypes.c_int
+        lib.rla_set_peer_wait_limit.argtypes = [ctypes.c_uint64]
+        lib.rla_set_peer_wait_limit.restype = ctypes.c_int
+        lib.rla_peer_alloc.argtypes = [sz, pp]
+        lib.rla_peer_alloc.restype = ctypes.c_int
+        lib.rla_peer_free.argtypes = [p]
+        lib.rla_peer_free.restype = ctypes.c_int
+        lib.rla_ipc_export.argtypes = [p, p]
+        lib.rla_ipc_export.restype = ctypes.c_int
+        lib.rla_ipc_open.argtypes = [p, pp]
+        lib.rla_ipc_open.restype = ctypes.c_int
+        lib.rla_ipc_close.argtypes = [p]
+        lib.rla_ipc_close.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -187,6 +208,71 @@ def set_decode_kernel(name: str) -> None:
     selector's choice), "skinny" or "stream".  For A/B runs and tests."""
     kid = 0 if name == "auto" else KERNEL_IDS[name]
     _check(load_library().rla_set_decode_kernel(kid), "rla_set_decode_kernel")
+
+
+def w8a16_gemm_allgather(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor, bias,
+                         out: torch.Tensor, recv_ptrs, recv_bytes: int, sync_ptr: int, rank: int) -> torch.Tensor:
+    """Column-parallel decode GEMM with the peer-to-peer all-gather fused in
+    (``rla_w8a16_gemm_allgather``): this rank's slice ``[M, n_local]`` goes to
+    columns ``[rank * n_local, (rank + 1) * n_local)`` of ``out`` and, as
+    flagged words, into every peer's receive buffer; the peers' slices are
+    unpacked from ``recv_ptrs[rank]`` into ``out``.  ``recv_ptrs``: every
+    rank's receive buffer as mapped in this process.  Raises ``RlaError``
+    (status 2) for shapes that are not decode shapes."""
+    lib = load_library()
+    M, K = x2d.shape
+    n_local = weight_int8.shape[0]
+    world = len(recv_ptrs)
+    recv = (ctypes.c_void_p * world)(*recv_ptrs)
+    stream = torch.cuda.current_stream(x2d.device).cuda_stream
+    need = lib.rla_w8a16_workspace_size(M, n_local, K)
+    ws_ptr, ws_bytes = None, 0
+    if need:
+        ws = _workspace(x2d.device, stream, need)
+        ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(x2d.device):
+        st = lib.rla_w8a16_gemm_allgather(
+            x2d.data_ptr(), x2d.stride(0), weight_int8.data_ptr(), weight_int8.stride(0), scale.data_ptr(),
+            _scale_dtype(scale), bias.data_ptr() if bias is not None else None, _bias_dtype(bias),
+            out.data_ptr(), out.stride(0), M, n_local, K, recv, recv_bytes, sync_ptr, rank, world,
+            ws_ptr, ws_bytes, stream)
+    _check(st, "rla_w8a16_gemm_allgather")
+    return out
+
+
+def set_peer_wait_limit(seconds: float) -> None:
+    """Limit of every wait inside the fused exchange (process-wide)."""
+    _check(load_library().rla_set_peer_wait_limit(int(seconds * 1e9)), "rla_set_peer_wait_limit")
+
+
+def peer_alloc(nbytes: int) -> int:
+    """Zeroed device buffer with its own allocation (IPC-exportable as a whole)."""
+    ptr = ctypes.c_void_p(0)
+    _check(load_library().rla_peer_alloc(nbytes, ctypes.byref(ptr)), "rla_peer_alloc")
+    return int(ptr.value)
+
+
+def peer_free(ptr: int) -> None:
+    _check(load_library().rla_peer_free(ptr), "rla_peer_free")
+
+
+def ipc_export(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(load_library().rla_ipc_export(ptr, buf), "rla_ipc_export")
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle has {IPC_HANDLE_BYTES} bytes, got {len(handle)}")
+    buf = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    ptr = ctypes.c_void_p(0)
+    _check(load_library().rla_ipc_open(buf, ctypes.byref(ptr)), "rla_ipc_open")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(load_library().rla_ipc_close(ptr), "rla_ipc_close")
 
 
 def launch_count() -> int:

@@ -26,7 +26,7 @@ void set_error(const char* fmt, ...) {
 
 static constexpr int kNumSMs = 148;  // B200; refined from the device at run time
 
-static int device_sm_count() {
+int device_sm_count() {
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kNumSMs;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return kNumSMs;

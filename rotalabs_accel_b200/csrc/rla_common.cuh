@@ -26,6 +26,8 @@ enum : unsigned int {
   RLA_DEVERR_TIMEOUT_A_EMPTY = 4,
   RLA_DEVERR_TIMEOUT_ACCUM = 5,
   RLA_DEVERR_TIMEOUT_SPLITK = 6,
+  RLA_DEVERR_TIMEOUT_PEER_DATA = 7,  // a peer's slice of an exchange call did not arrive
+  RLA_DEVERR_TIMEOUT_GRID = 8,       // CTAs of an exchange launch did not all finish their slice
 };
 
 // One second: far above any legitimate wait inside one launch.

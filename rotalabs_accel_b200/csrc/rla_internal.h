@@ -1,6 +1,7 @@
 // Internal declarations shared by the library's translation units.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -8,6 +9,28 @@
 #include "../../include/rla_w8a16.h"
 
 namespace rla {
+
+// Direct peer-to-peer output exchange of the column-parallel layer (one
+// process per GPU, every rank's receive buffer IPC-mapped into every other
+// rank; protocol in rla_peer.cuh).  world == 0: no exchange.
+constexpr int kMaxPeers = 8;
+// Sync area of one rank (local, never mapped by peers): 32-bit words.
+constexpr int kSyncSeq = 0;        // exchange calls this rank has completed
+constexpr int kSyncArrive = 32;    // CTAs of the running call that finished phase 1
+constexpr int kSyncUnpacked = 64;  // unpacking CTAs of the running call that are done
+constexpr int kSyncAbort = 96;     // call number whose wait gave up (stops the other waits)
+constexpr size_t kSyncBytes = 512;
+
+struct PeerOut {
+  uint2* recv[kMaxPeers];       // rank d's receive buffer: 2 halves (call parity) of flagged words
+  unsigned int* sync;           // this rank's sync area
+  int64_t half_words;           // flagged words per parity half
+  int64_t slot_words;           // words of one source rank's slice in this call: ceil(M/2) * n_local
+  unsigned long long wait_ns;   // limit of every wait
+  unsigned int unpackers;       // R: CTAs that unpack peer slices (1 <= R <= CTAs of the launch)
+  int world;
+  int rank;
+};
 
 // Arguments common to every W8A16 GEMM kernel.
 struct GemmArgs {
@@ -22,6 +45,9 @@ struct GemmArgs {
   void* y;
   int64_t ldy;
   int M, N, K;
+  // world == 0 unless the call is rla_w8a16_gemm_allgather; then y is the
+  // full [M, world * n_local] output and N = n_local.
+  PeerOut peer{};
 };
 
 // A launch plan chosen by the per-shape selector.
@@ -50,6 +76,7 @@ constexpr int kMaxSplitRowBlocks = static_cast<int>(kSplitCounterBytes / sizeof(
 Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace);
 
 void note_launch();
+int device_sm_count();  // SMs of the current device (148 if it cannot be read)
 void set_error(const char* fmt, ...);
 
 cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);

@@ -6,3 +6,4 @@
 #include "rla_tc.cu"
 #include "rla_capi.cu"
 #include "rla_noalloc.cu"
+#include "rla_peer.cu"

@@ -1,0 +1,158 @@
+// Device side of the direct peer-to-peer output exchange (column-parallel
+// decode over several GPUs, one process per GPU).
+//
+// Every rank runs the same sequence of exchange calls; rank r computes output
+// columns [r * n_local, (r + 1) * n_local) of every row.  Call s of rank r:
+//
+//  * Phase 1 (the GEMM's epilogue).  Each output element of r's slice goes
+//    to r's own y with a plain store, and to every peer d as part of an 8-byte
+//    "flagged word" {fp16 y[2p][n], fp16 y[2p+1][n], s} stored over NVLink into
+//    d's receive buffer.  An aligned 8-byte store is seen whole or not at
+//    all, so a reader that finds the flag s in a word has its data: no fence,
+//    no separate completion flag (the low-latency protocol NCCL calls LL).
+//  * Phase 2 (unpacking).  Every CTA takes a ticket when its phase 1 is done.
+//    The last R CTAs to finish wait until all CTAs of the launch have taken
+//    one, then poll the receive buffer for every peer's words of call s and
+//    write them into y.  When the kernel completes, y holds all slices.
+//
+// Reuse without a handshake: receive buffers are double-buffered by the
+// parity of s.  A rank writes a peer's parity-p half in call s only after its
+// own call s - 1 has completed, which needed the peer's words of call s - 1,
+// which the peer wrote after its call s - 2 -- the last reader of that half --
+// had completed.  Stale words carry older call numbers.  (Every phase-1 store
+// comes after the kernel's dependency wait, so this holds with programmatic
+// dependent launch too.)
+//
+// No cross-GPU deadlock: a CTA waits on peers only after every CTA of its own
+// launch has finished phase 1, and phase 1 waits on nothing outside the GPU.
+// Inside the GPU, R <= (resident CTAs + 1) / 2 (or the whole grid when it is
+// resident at once) leaves room for every CTA that has not yet run.
+//
+// The call number s is one more than the calls this rank has completed (a
+// counter in its sync area, advanced by the last unpacking CTA).  Every wait is
+// bounded by PeerOut::wait_ns; a wait that gives up records a device error and
+// marks the call aborted (the other waits of the call stop at once; y is then
+// incomplete).
+#pragma once
+
+#include "rla_common.cuh"
+#include "rla_internal.h"
+
+namespace rla {
+
+RLA_DEVFN unsigned int rla_ld_relaxed_gpu_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// One flagged word {data, flag}: 8-byte aligned, written and read whole.
+RLA_DEVFN void rla_st_flagged(uint2* p, uint32_t data, uint32_t flag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(flag) : "memory");
+}
+RLA_DEVFN uint2 rla_ld_flagged(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+// This launch's call number.  Read after the dependency wait: the previous
+// exchange call in the stream has completed and advanced the counter.
+RLA_DEVFN unsigned int peer_call(const PeerOut& po) { return rla_ld_relaxed_gpu_u32(po.sync + kSyncSeq) + 1u; }
+
+// Flagged word (pair p, column n) of `src`'s slice in rank d's receive buffer.
+RLA_DEVFN uint2* peer_word(const PeerOut& po, int d, unsigned int s, int src, int64_t pair_col) {
+  return po.recv[d] + (int64_t)(s & 1u) * po.half_words + (int64_t)src * po.slot_words + pair_col;
+}
+
+// Phase 1 for rows (2p, 2p+1) of local column n: this rank's y directly,
+// every peer one flagged word.  v1 is ignored when row 2p+1 does not exist.
+RLA_DEVFN void peer_store_pair(const PeerOut& po, unsigned int s, __half* y, int64_t ldy, int M, int n_local, int p,
+                               int n, __half v0, __half v1) {
+  const int m = 2 * p;
+  const int64_t col = (int64_t)po.rank * n_local + n;
+  y[(int64_t)m * ldy + col] = v0;
+  if (m + 1 < M) y[(int64_t)(m + 1) * ldy + col] = v1;
+  const uint32_t data = static_cast<uint32_t>(__half_as_ushort(v0)) |
+                        (static_cast<uint32_t>(__half_as_ushort(v1)) << 16);
+  const int64_t pc = (int64_t)p * n_local + n;
+  for (int d = 0; d < po.world; ++d)
+    if (d != po.rank) rla_st_flagged(peer_word(po, d, s, po.rank, pc), data, s);
+}
+
+// Bounded wait for one flagged word of call s (t0: start of the wait phase).
+RLA_DEVFN bool peer_wait_word(const PeerOut& po, const uint2* w, unsigned int s, uint2& out, uint64_t t0) {
+  out = rla_ld_flagged(w);
+  if (out.y == s) return true;
+  const unsigned int* abort_word = po.sync + kSyncAbort;
+  while (true) {
+    __nanosleep(100);
+    out = rla_ld_flagged(w);
+    if (out.y == s) return true;
+    if (rla_ld_relaxed_gpu_u32(abort_word) == s) return false;  // another wait of this call gave up
+    if (rla_globaltimer() - t0 > po.wait_ns) {
+      rla_record_error(RLA_DEVERR_TIMEOUT_PEER_DATA);
+      atomicExch(po.sync + kSyncAbort, s);
+      return false;
+    }
+  }
+}
+
+// Phase 2.  Called by the `nthreads` threads of a CTA that take part in named
+// barrier `bar_id` (thread index tid), after their last phase-1 store; `slot`
+// is a shared-memory int of the CTA.
+RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t ldy, int M, int n_local, int tid,
+                           int nthreads, int bar_id, int* slot) {
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
+  const unsigned int ctas = gridDim.x * gridDim.y;
+  const unsigned int R = po.unpackers;
+  if (tid == 0) {
+    const unsigned int ticket = atomicAdd(po.sync + kSyncArrive, 1u);
+    *slot = ticket >= ctas - R ? static_cast<int>(ticket - (ctas - R)) : -1;
+  }
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
+  const int u = *slot;
+  if (u < 0) return;  // not an unpacker: this CTA is done
+  const uint64_t t0 = rla_globaltimer();
+  if (tid == 0) {
+    // Wait until every CTA of the launch has finished phase 1.
+    while (rla_ld_relaxed_gpu_u32(po.sync + kSyncArrive) < ctas) {
+      if (rla_ld_relaxed_gpu_u32(po.sync + kSyncAbort) == s) break;
+      if (rla_globaltimer() - t0 > po.wait_ns) {
+        rla_record_error(RLA_DEVERR_TIMEOUT_GRID);
+        atomicExch(po.sync + kSyncAbort, s);
+        break;
+      }
+      __nanosleep(100);
+    }
+  }
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
+  const int pairs = (M + 1) / 2;
+  const int64_t per_src = (int64_t)pairs * n_local;
+  const int64_t total = per_src * (po.world - 1);
+  for (int64_t w = (int64_t)u * nthreads + tid; w < total; w += (int64_t)R * nthreads) {
+    const int si = static_cast<int>(w / per_src);
+    const int src = si < po.rank ? si : si + 1;
+    const int64_t pc = w - (int64_t)si * per_src;
+    uint2 v;
+    if (!peer_wait_word(po, peer_word(po, po.rank, s, src, pc), s, v, t0)) break;
+    const int p = static_cast<int>(pc / n_local);
+    const int n = static_cast<int>(pc - (int64_t)p * n_local);
+    const int64_t col = (int64_t)src * n_local + n;
+    y[(int64_t)(2 * p) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x & 0xffffu));
+    if (2 * p + 1 < M) y[(int64_t)(2 * p + 1) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x >> 16));
+  }
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
+  if (tid == 0) {
+    const unsigned int done = atomicAdd(po.sync + kSyncUnpacked, 1u);
+    if (done == R - 1) {
+      // Last unpacker: every CTA has taken its ticket and every unpacker has
+      // stopped reading the counters; the next launch reads them only after
+      // this one has completed.
+      po.sync[kSyncArrive] = 0u;
+      po.sync[kSyncUnpacked] = 0u;
+      po.sync[kSyncSeq] = s;
+    }
+  }
+}
+
+}  // namespace rla

@@ -25,8 +25,13 @@
 // Launched with programmatic dependent launch: a CTA warms L2 with its first
 // weight bytes while the previous kernel in the stream finishes, and reads
 // nothing before that kernel is done (rla_griddep_wait).
+//
+// With a peer exchange (PEER, rla_w8a16_gemm_allgather) the epilogue stores
+// pairs of rows into y and, as flagged words, into every peer's receive
+// buffer, and every CTA ends with peer_finish (rla_peer.cuh).
 #include "rla_common.cuh"
 #include "rla_internal.h"
+#include "rla_peer.cuh"
 
 namespace rla {
 
@@ -35,12 +40,13 @@ struct XFrag {
   uint4 v[NT][2];
 };
 
-template <int NT, int WN, int WK, int U>
+template <int NT, int WN, int WK, int U, bool PEER>
 __global__ void __launch_bounds__(32 * WN * WK)
     w8a16_skinny_kernel(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,
                         const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias,
                         int bias_kind, __half* __restrict__ y, int64_t ldy, int M, int N, int K,
-                        int chunks_per_split, float* __restrict__ partial, unsigned int* __restrict__ counters) {
+                        int chunks_per_split, float* __restrict__ partial, unsigned int* __restrict__ counters,
+                        const __grid_constant__ PeerOut po) {
   constexpr int ROWS = 16 * WN;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -85,6 +91,9 @@ __global__ void __launch_bounds__(32 * WN * WK)
     }
   }
   rla_griddep_wait();
+  unsigned int call = 0;
+  if constexpr (PEER) call = peer_call(po);
+  __shared__ int peer_slot;
 
   const uint4 zero4 = make_uint4(0, 0, 0, 0);
   for (int c = c_begin + wk; c < c_end; c += WK * U) {
@@ -159,14 +168,23 @@ __global__ void __launch_bounds__(32 * WN * WK)
                          : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias)[n])
                                           : static_cast<const float*>(bias)[n];
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
+        for (int t = 0; t < NT; ++t) {
+          if constexpr (PEER) {
+            // rows 8t + 2q and 8t + 2q + 1 form pair 4t + q
+            if (t * 8 + 2 * q < M)
+              peer_store_pair(po, call, y, ldy, M, N, 4 * t + q, n, __float2half_rn(fmaf(acc[t][2 * hi], sc, bi)),
+                              __float2half_rn(fmaf(acc[t][2 * hi + 1], sc, bi)));
+          } else {
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int m = t * 8 + 2 * q + j;
-            if (m < M) y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(acc[t][2 * hi + j], sc, bi));
+            for (int j = 0; j < 2; ++j) {
+              const int m = t * 8 + 2 * q + j;
+              if (m < M) y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(acc[t][2 * hi + j], sc, bi));
+            }
           }
+        }
       }
     }
+    if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
     return;
   }
 
@@ -194,13 +212,18 @@ __global__ void __launch_bounds__(32 * WN * WK)
     is_last = (prev == gridDim.y - 1);
   }
   __syncthreads();
-  if (!is_last) return;
+  if (!is_last) {
+    if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
+    return;
+  }
   __threadfence();
 
   const int rows_here = min(ROWS, N - row_base);
-  for (int idx = threadIdx.x; idx < rows_here * M; idx += blockDim.x) {
+  // Plain output: one element per step; exchange: one pair of rows per step.
+  const int steps = PEER ? (M + 1) / 2 : M;
+  for (int idx = threadIdx.x; idx < rows_here * steps; idx += blockDim.x) {
     const int n = row_base + idx % rows_here;
-    const int m = idx / rows_here;
+    const int m = (PEER ? 2 : 1) * (idx / rows_here);
     float sum = 0.f;
     for (int sidx = 0; sidx < (int)gridDim.y; ++sidx) sum += __ldcg(partial + ((int64_t)sidx * M + m) * N + n);
     const float sc =
@@ -208,9 +231,19 @@ __global__ void __launch_bounds__(32 * WN * WK)
     const float bi = bias_kind == 0 ? 0.f
                      : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias)[n])
                                       : static_cast<const float*>(bias)[n];
-    y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(sum, sc, bi));
+    if constexpr (PEER) {
+      float sum1 = 0.f;
+      if (m + 1 < M)
+        for (int sidx = 0; sidx < (int)gridDim.y; ++sidx)
+          sum1 += __ldcg(partial + ((int64_t)sidx * M + m + 1) * N + n);
+      peer_store_pair(po, call, y, ldy, M, N, m / 2, n, __float2half_rn(fmaf(sum, sc, bi)),
+                      __float2half_rn(fmaf(sum1, sc, bi)));
+    } else {
+      y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(sum, sc, bi));
+    }
   }
   if (threadIdx.x == 0) counters[blockIdx.x] = 0u;  // leave the workspace re-usable
+  if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
 }
 
 template <int NT, int WN, int WK, int U>
@@ -233,9 +266,24 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, w8a16_skinny_kernel<NT, WN, WK, U>, static_cast<const __half*>(a.x), a.ldx, a.w,
+  auto kern = a.peer.world > 0 ? w8a16_skinny_kernel<NT, WN, WK, U, true> : w8a16_skinny_kernel<NT, WN, WK, U, false>;
+  PeerOut po = a.peer;
+  if (po.world > 0) {
+    // Unpacking CTAs: the whole grid when it is resident at once, else at
+    // most (resident + 1) / 2 so that the CTAs still to run find room.
+    static int per_sm = -1;
+    if (per_sm < 0) {
+      int v = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, 32 * WN * WK, 0) != cudaSuccess || v < 1) v = 1;
+      per_sm = v;
+    }
+    const unsigned int ctas = static_cast<unsigned int>(p.grid_x) * static_cast<unsigned int>(p.splits);
+    const unsigned int resident = static_cast<unsigned int>(per_sm * device_sm_count());
+    po.unpackers = ctas <= resident ? ctas : (resident + 1) / 2;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<const __half*>(a.x), a.ldx, a.w,
                             a.ldw, a.scale, a.scale_f32, a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M,
-                            a.N, a.K, cps, partial, counters);
+                            a.N, a.K, cps, partial, counters, po);
 }
 
 // Instantiated configurations: NT in {1, 2, 4}; (WN, WK) in {(1, 8), (2, 4), (4, 2)}.

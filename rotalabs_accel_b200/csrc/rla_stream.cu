@@ -43,9 +43,17 @@
 //    copy engine ahead of the running kernel's loads.)
 //
 // Waits are bounded (rla_mbar_wait); on a timeout the CTA records a device
-// error, raises its abort flag and returns.
+// error and raises its abort flag: the producer stops issuing copies (and
+// waits, bounded, for those in flight), the consumers run the rest of their
+// loop without waiting or computing, so every named barrier still completes.
+//
+// With a peer exchange (PEER, rla_w8a16_gemm_allgather) the epilogue stores
+// pairs of rows into y and, as flagged words, into every peer's receive
+// buffer, and the consumer warps end with peer_finish (rla_peer.cuh), also
+// after an abort.
 #include "rla_common.cuh"
 #include "rla_internal.h"
+#include "rla_peer.cuh"
 #include "rla_tmap.cuh"
 
 namespace rla {
@@ -97,12 +105,12 @@ RLA_DEVFN int sk_owner(int64_t units, int64_t u, int P) {
   return p;
 }
 
-template <int NT>
+template <int NT, bool PEER>
 __global__ void __launch_bounds__(sk::THREADS, 1)
     w8a16_stream_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias, int bias_kind,
                         __half* __restrict__ y, int64_t ldy, int M, int N, int K, float* __restrict__ partial,
-                        unsigned int* __restrict__ counters) {
+                        unsigned int* __restrict__ counters, const __grid_constant__ PeerOut po) {
   using Cfg = StreamCfg<NT>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int SB = Cfg::SB;
@@ -215,6 +223,8 @@ __global__ void __launch_bounds__(sk::THREADS, 1)
     for (int t = 0; t < NT; ++t) acc[e][t][0] = acc[e][t][1] = acc[e][t][2] = acc[e][t][3] = 0.f;
 
   rla_griddep_wait();
+  unsigned int call = 0;
+  if constexpr (PEER) call = peer_call(po);
   int64_t f = f_begin;
   int rb = rb_begin, c0 = c_begin;
   int rb_loaded = -1;
@@ -222,9 +232,12 @@ __global__ void __launch_bounds__(sk::THREADS, 1)
   for (int it = 0; f < f_end; ++it) {
     const int nb = static_cast<int>(imin64(min(SB, c_count - c0), f_end - f));
     const int s = it % STAGES;
+    // After an abort (a wait that gave up, here or in another warp) the warp
+    // skips the stage's math but keeps the loop's control flow, so every
+    // consumer warp still takes every named barrier of the CTA.
     int ok = 1;
     if (lane == 0) ok = rla_mbar_wait(&full[s], (it / STAGES) & 1, RLA_DEVERR_TIMEOUT_TMA_FULL, abort_flag) ? 1 : 0;
-    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
     if (rb != rb_loaded) {
       // Start of a row block: fetch its scale / bias now, used at its end.
       rb_loaded = rb;
@@ -241,7 +254,7 @@ __global__ void __launch_bounds__(sk::THREADS, 1)
     const uint8_t* stg = stages + (size_t)s * Cfg::STAGE;
 #pragma unroll
     for (int b = 0; b < SB; ++b) {
-      if (b >= nb) break;
+      if (b >= nb || !ok) break;
       const uint8_t* wb = stg + b * sk::W_BOX;
       const uint4 a0 = *reinterpret_cast<const uint4*>(wb + wrowA + wc0);
       const uint4 a1 = *reinterpret_cast<const uint4*>(wb + wrowA + wc1);
@@ -275,7 +288,7 @@ __global__ void __launch_bounds__(sk::THREADS, 1)
       }
     }
     __syncwarp();
-    if (lane == 0) rla_mbar_arrive(&empty[s]);
+    if (lane == 0 && ok) rla_mbar_arrive(&empty[s]);
     f += nb;
     c0 += nb;
     const bool rb_done = c0 == c_count;
@@ -373,14 +386,29 @@ __global__ void __launch_bounds__(sk::THREADS, 1)
         const int n = rb_cur * sk::RB + rl0 + 8 * hi;
         if (n >= N) continue;
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
+        for (int t = 0; t < NT; ++t) {
+          if constexpr (PEER) {
+            // rows 8t + 2q and 8t + 2q + 1 form pair 4t + q
+            if (t * 8 + 2 * q < M)
+              peer_store_pair(po, call, y, ldy, M, N, 4 * t + q, n,
+                              __float2half_rn(fmaf(sum[t][2 * hi], sc_pre[hi], bi_pre[hi])),
+                              __float2half_rn(fmaf(sum[t][2 * hi + 1], sc_pre[hi], bi_pre[hi])));
+          } else {
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const int m = t * 8 + 2 * q + jj;
-            if (m < M) y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(sum[t][2 * hi + jj], sc_pre[hi], bi_pre[hi]));
+            for (int jj = 0; jj < 2; ++jj) {
+              const int m = t * 8 + 2 * q + jj;
+              if (m < M) y[(int64_t)m * ldy + n] = __float2half_rn(fmaf(sum[t][2 * hi + jj], sc_pre[hi], bi_pre[hi]));
+            }
           }
+        }
       }
     }
+  }
+  if constexpr (PEER) {
+    // Every consumer warp gets here (after the loop, also after an abort: all
+    // its waits are bounded), so the barriers over the consumers complete.
+    __shared__ int peer_slot;
+    peer_finish(po, call, y, ldy, M, N, threadIdx.x - 32, NCW * 32, 3, &peer_slot);
   }
 }
 
@@ -398,7 +426,10 @@ static cudaError_t launch_stream_nt(const GemmArgs& a, const Plan& p, void* work
   if (!make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx * 2,
                     64, Cfg::XR, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  auto kern = w8a16_stream_kernel<NT>;
+  auto kern = a.peer.world > 0 ? w8a16_stream_kernel<NT, true> : w8a16_stream_kernel<NT, false>;
+  // At most one CTA per SM, all resident at once: every CTA unpacks a share.
+  PeerOut po = a.peer;
+  if (po.world > 0) po.unpackers = static_cast<unsigned int>(p.grid_x);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM);
   if (e != cudaSuccess) return e;
   unsigned int* counters = static_cast<unsigned int*>(workspace);
@@ -414,7 +445,7 @@ static cudaError_t launch_stream_nt(const GemmArgs& a, const Plan& p, void* work
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, tw, tx, a.scale, a.scale_f32, a.bias, a.bias_kind, static_cast<__half*>(a.y),
-                            a.ldy, a.M, a.N, a.K, partial, counters);
+                            a.ldy, a.M, a.N, a.K, partial, counters, po);
 }
 
 cudaError_t launch_stream(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s) {

@@ -1,0 +1,157 @@
+"""Direct peer-to-peer output exchange for the column-parallel layer.
+
+rotalabs-accel has no distributed code; this is the fused output step of the
+sharded ``Int8Linear`` (src/rotalabs_accel/kernels/gemm.py:241-336 with its
+output channels split over the ranks).  Instead of "local GEMM, then
+``all_gather_into_tensor``, then a reorder kernel", one decode kernel per
+rank computes its column slice, writes it into its own output and sends it
+to every peer over NVLink as 8-byte flagged words {two fp16 values, call
+number}; the kernel's last CTAs unpack the peers' slices from this rank's
+receive buffer (``rla_w8a16_gemm_allgather``).  No host synchronisation,
+no separate collective, one launch.
+
+Set-up is collective (every rank of the group, one process per GPU, one
+node): ``PeerExchange(group, max_rows, max_n_local)`` allocates this rank's
+receive buffer with the library's own ``cudaMalloc`` (so an IPC handle covers
+exactly that buffer), exchanges the handles in one all-gather of a few bytes
+over the process group, maps every peer's buffer, and keeps a local sync
+area.  ``exchange.gemm(x2d, weight_int8, scale, bias)`` then runs on every
+rank, in the same order and with the same shapes on every rank,
+stream-ordered on each rank.  ``close()`` (collective) unmaps and frees.
+"""
+
+from __future__ import annotations
+
+import struct
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _capi
+
+
+def exchange_blobs(blob: bytes, group: Optional[dist.ProcessGroup] = None) -> List[bytes]:
+    """All-gather one byte string per rank (all the same length) over the
+    process group (NCCL or gloo); returns them in rank order."""
+    world = dist.get_world_size(group)
+    backend = dist.get_backend(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    mine = torch.tensor(list(blob), dtype=torch.uint8, device=dev)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine, group=group)
+    return [bytes(p.cpu().tolist()) for p in parts]
+
+
+def receive_bytes(world: int, max_rows: int, max_n_local: int) -> int:
+    """Receive buffer size for calls of up to ``max_rows`` rows and
+    ``max_n_local`` columns per rank: two halves (call parity) of
+    ``world * ceil(max_rows / 2) * max_n_local`` 8-byte flagged words."""
+    return 16 * world * ((max_rows + 1) // 2) * max_n_local
+
+
+class _SharedBuffer:
+    """One device buffer per rank, every rank's mapped into this process.
+    Every step is collective: a rank whose set-up fails still takes part in
+    both exchanges, and then every rank raises (none is left half set up)."""
+
+    def __init__(self, nbytes: int, group, rank: int, header: bytes):
+        self.local = 0
+        self.ptrs: List[int] = []
+        self._opened: List[int] = []
+        error = None
+        handle = bytes(_capi.IPC_HANDLE_BYTES)
+        try:
+            self.local = _capi.peer_alloc(nbytes)
+            handle = _capi.ipc_export(self.local)
+        except Exception as e:  # noqa: BLE001 - reported on every rank below
+            error = e
+        blobs = exchange_blobs(header + handle, group)
+        if error is None:
+            try:
+                for r, b in enumerate(blobs):
+                    if b[:len(header)] != header:
+                        raise RuntimeError(f"peer exchange: rank {r} set up a different exchange than rank {rank}")
+                    if r == rank:
+                        self.ptrs.append(self.local)
+                    else:
+                        p = _capi.ipc_open(b[len(header):])
+                        self._opened.append(p)
+                        self.ptrs.append(p)
+            except Exception as e:  # noqa: BLE001
+                error = e
+        oks = exchange_blobs(b"\x01" if error is None else b"\x00", group)
+        if error is not None or any(o != b"\x01" for o in oks):
+            self.release()
+            if error is not None:
+                raise error
+            bad = [r for r, o in enumerate(oks) if o != b"\x01"]
+            raise RuntimeError(f"peer exchange: set-up failed on rank(s) {bad}")
+
+    def unmap(self) -> None:
+        """Close this process's mappings of the peers' buffers."""
+        for p in self._opened:
+            _capi.ipc_close(p)
+        self._opened = []
+        self.ptrs = []
+
+    def release(self) -> None:
+        self.unmap()
+        if self.local:
+            _capi.peer_free(self.local)
+            self.local = 0
+
+
+class PeerExchange:
+    """Receive buffers and sync area of a process group for
+    ``rla_w8a16_gemm_allgather`` (decode calls of up to ``max_rows`` rows and
+    ``max_n_local`` output columns per rank)."""
+
+    def __init__(self, group: Optional[dist.ProcessGroup] = None, max_rows: int = 32, max_n_local: int = 8192):
+        if not dist.is_initialized():
+            raise RuntimeError("PeerExchange needs an initialised process group")
+        if not 1 <= max_rows <= 32 or max_n_local < 1:
+            raise ValueError("PeerExchange: need 1 <= max_rows <= 32 (the decode kernels) and max_n_local >= 1")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _capi.MAX_PEERS:
+            raise ValueError(f"the peer exchange supports at most {_capi.MAX_PEERS} ranks, got {self.world}")
+        self.max_rows, self.max_n_local = max_rows, max_n_local
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.recv_bytes = receive_bytes(self.world, max_rows, max_n_local)
+        header = struct.pack("<qqq", self.world, max_rows, max_n_local)
+        self._recv = _SharedBuffer(self.recv_bytes, group, self.rank, header)
+        self._sync = torch.zeros(_capi.PEER_SYNC_BYTES // 4, dtype=torch.int32, device=self.device)
+
+    def calls_completed(self) -> int:
+        """Exchange calls this rank has completed (synchronises)."""
+        return int(self._sync[0].item())
+
+    def gemm(self, x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
+             bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``out[M, world * n_local]``: every rank's slice of ``x2d @
+        (weight_int8 * scale[:, None]).T (+ bias)``, this rank's computed
+        here from its shard ``weight_int8 [n_local, K]``."""
+        if self._recv is None:
+            raise RuntimeError("PeerExchange is closed")
+        M = x2d.shape[0]
+        n_local = weight_int8.shape[0]
+        if M > self.max_rows or n_local > self.max_n_local:
+            raise ValueError(f"exchange sized for {self.max_rows} rows x {self.max_n_local} columns per rank, "
+                             f"got {M} x {n_local}")
+        if out is None:
+            out = torch.empty((M, self.world * n_local), dtype=torch.float16, device=x2d.device)
+        return _capi.w8a16_gemm_allgather(x2d, weight_int8, scale, bias, out, self._recv.ptrs, self.recv_bytes,
+                                          self._sync.data_ptr(), self.rank)
+
+    def close(self) -> None:
+        """Collective: wait for every rank's work, then unmap and free."""
+        if self._recv is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)       # no peer writes into our buffer after this
+        self._recv.unmap()
+        dist.barrier(group=self.group)       # no rank maps another's buffer any more
+        self._recv.release()
+        self._recv = None

@@ -7,12 +7,18 @@ channels are split over the ranks: rank r holds rows
 ``n_local = ceil(N / world)`` (the last shard is zero-padded when ``world``
 does not divide ``N``).  Every rank has the whole activation ``x``.
 
-Forward, per rank:
+Forward, per rank, collective path:
   1. ``y_local[M, n_local]`` = the sm_100a W8A16 kernel on the local shard;
   2. one ``all_gather_into_tensor`` of the slices into
      ``staging[world, M, n_local]`` (NCCL over NVLink on GPUs, gloo on the CPU);
   3. ``rla_gather_columns`` reorders the staging buffer into ``y[M, N]``
      (skipped when M == 1: the staging layout already is ``[1, N]``).
+
+Fused path (after ``enable_peer_exchange``; decode batches of at most
+``max_tokens`` rows, K % 16 == 0): one kernel per rank computes its slice,
+sends it to every peer over NVLink and unpacks theirs
+(``rotalabs_accel_b200.peer``).  The choice depends only on shapes, which
+are the same on every rank, so the ranks always take the same path.
 
 Per-channel quantization is row-independent, so quantizing a shard gives
 exactly the rows the full quantization would.
@@ -26,6 +32,7 @@ import torch
 import torch.distributed as dist
 
 from .gemm import int8_gemm
+from .peer import PeerExchange
 from .quantization import quantize_weight_per_channel
 
 
@@ -92,7 +99,8 @@ class ColumnParallelInt8Linear(torch.nn.Module):
         else:
             self.register_parameter("bias", None)
         self._quantized = False
-        self._staging = None
+        self._exchange: Optional[PeerExchange] = None
+        self._owns_exchange = False
 
     def _check_agreement(self) -> None:
         """Every rank must shard the same layer: compare (in, out, world) over
@@ -136,12 +144,48 @@ class ColumnParallelInt8Linear(torch.nn.Module):
             self.bias.data[:rows].copy_(bias[self.start:self.stop])
         self._quantized = True
 
+    def enable_peer_exchange(self, max_tokens: int = 32, exchange: Optional[PeerExchange] = None) -> None:
+        """Collective (every rank, module already on its GPU): use the fused
+        peer-to-peer path for batches of up to ``max_tokens`` rows (at most
+        32).  ``exchange`` may be shared by several layers (it must be sized
+        for this layer's rows and columns per rank); by default the layer
+        makes its own."""
+        if not 1 <= max_tokens <= 32:
+            raise ValueError("max_tokens must be in [1, 32] (the decode kernels)")
+        if not self.weight_int8.is_cuda:
+            raise RuntimeError("enable_peer_exchange: move the module to its GPU first")
+        if exchange is None:
+            exchange = PeerExchange(self.group, max_rows=max_tokens, max_n_local=self.n_local)
+            self._owns_exchange = True
+        elif exchange.max_rows < max_tokens or exchange.max_n_local < self.n_local:
+            raise ValueError("enable_peer_exchange: the shared exchange is too small for this layer")
+        self._exchange = exchange
+        self._max_tokens = max_tokens
+
+    def close_peer_exchange(self) -> None:
+        """Collective: release the fused path's buffers (when the layer owns them)."""
+        if self._exchange is not None and self._owns_exchange:
+            self._exchange.close()
+        self._exchange = None
+        self._owns_exchange = False
+
+    def _fused_ok(self, x2: torch.Tensor) -> bool:
+        return (self._exchange is not None and x2.is_cuda and x2.dtype == torch.float16
+                and 1 <= x2.shape[0] <= self._max_tokens and self.in_features % 16 == 0)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not self._quantized:
             raise RuntimeError("Weights not quantized. Call quantize_weights() first.")
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.in_features)
         M = x2.shape[0]
+        if self._fused_ok(x2):
+            if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+                x2 = x2.clone(memory_format=torch.contiguous_format)
+            y = self._exchange.gemm(x2, self.weight_int8, self.scale, self.bias)
+            if y.shape[1] != self.out_features:
+                y = y[:, :self.out_features]
+            return y.reshape(*lead, self.out_features)
         y_local = int8_gemm(x2, self.weight_int8, self.scale, self.bias)
         if self.world == 1:
             return y_local[:, :self.out_features].reshape(*lead, self.out_features)
