@@ -335,14 +335,17 @@ def main():
         for _ in range(warmup):
             graph.replay()
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        # The clock sampler starts before the barrier: every rank must begin
+        # its timed replays together (a rank that starts late makes the
+        # others wait inside their first exchange, inside the timed region).
         sampler = ClockSampler(local_rank) if sample_clocks else None
         if sampler:
             sampler.start()
             time.sleep(0.3)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             e0.record(stream)

@@ -242,7 +242,7 @@ def _worker_multi(rank, world, port, q):
         q.put((rank, False, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_multi_gpu_fused_equals_nccl_path(cuda_lib, world):
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
