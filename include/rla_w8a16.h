@@ -232,6 +232,41 @@ RLA_API int rla_ipc_export(const void* ptr, void* handle);
 RLA_API int rla_ipc_open(const void* handle, void** ptr);
 RLA_API int rla_ipc_close(void* ptr);
 
+/*
+ * Gate and up projections of a SwiGLU MLP in one W8A16 GEMM, with the
+ * activation in the epilogue:
+ *
+ *     y[m, n] = fp16( silu(g) * u ),  g = fp16(scale_gate[n] * sum_k x[m,k] w_gate[n,k] (+ bias_gate[n])),
+ *                                     u = fp16(scale_up[n]   * sum_k x[m,k] w_up[n,k]   (+ bias_up[n])),
+ *     silu(g) = g * sigmoid(g), computed in fp32.
+ *
+ * Replaces rotalabs-accel's `int8_gemm(x, gate) ; int8_gemm(x, up) ;
+ * swiglu_fused(gate, up)` (src/rotalabs_accel/kernels/gemm.py:189-238 twice,
+ * then kernels/activations.py:109-137 -> the Triton kernel at :55-80, which
+ * computes silu(gate) * up in fp32 from the two fp16 outputs) with one
+ * launch and no [M, N] intermediates.  w_gate and w_up are int8 [N, K] with
+ * the same row stride ldw; scales [N] share scale_dtype, biases [N] share
+ * bias_dtype (both NULL with RLA_DTYPE_NONE).  Workspace as rla_w8a16_gemm,
+ * sized by rla_w8a16_swiglu_workspace_size.  Decode (M <= 32) runs the
+ * skinny kernel with gate and up rows in one MMA tile, prefill the tcgen05
+ * kernel with gate and up rows in one 128-lane TMEM tile.
+ */
+RLA_API int rla_w8a16_gemm_swiglu(const void* x, int64_t ldx, const int8_t* w_gate, const int8_t* w_up, int64_t ldw,
+                                  const void* scale_gate, const void* scale_up, int scale_dtype, const void* bias_gate,
+                                  const void* bias_up, int bias_dtype, void* y, int64_t ldy, int64_t M, int64_t N,
+                                  int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+RLA_API size_t rla_w8a16_swiglu_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/*
+ * RMSNorm of M fp16 rows of length K: y = fp16(x * rsqrt(mean(x^2) + eps) * w),
+ * the mean and product in fp32.  Replaces rotalabs-accel's CUDA RMSNorm
+ * (src/rotalabs_accel/kernels/normalization.py:186-213 -> the Triton kernel
+ * at :66-101); weight [K] is F32, F16 or BF16.  The normalisation in front of
+ * the gate/up GEMM of the MLP block.
+ */
+RLA_API int rla_rmsnorm(const void* x, int64_t ldx, const void* weight, int weight_dtype, float eps, void* y,
+                        int64_t ldy, int64_t M, int64_t K, void* stream);
+
 /* Number of kernels this library has launched in this process (all devices). */
 RLA_API uint64_t rla_launch_count(void);
 

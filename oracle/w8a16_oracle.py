@@ -15,6 +15,11 @@ W8A16 GEMM, step by step:
 * ``int8_gemm_torch``             <- src/rotalabs_accel/kernels/gemm.py:31-48
   (the reference's ``int8_gemm`` routes every non-CUDA call here,
   src/rotalabs_accel/kernels/gemm.py:234-238)
+* ``rmsnorm_torch``               <- src/rotalabs_accel/kernels/normalization.py:32-45
+* ``swiglu_torch``                <- src/rotalabs_accel/kernels/activations.py:36-46
+* ``swiglu_mlp``                  <- the MLP block of the benchmark's config 3 as
+  the reference composes it on the CPU: rmsnorm -> int8_gemm gate, up ->
+  swiglu -> int8_gemm down (kernels/activations.py:175-178 with Int8Linear)
 
 The reference's arithmetic lives in its third-party dependency torch
 (``torch>=2.0.0``, pyproject.toml:42, unpinned; 2.11.0 was used to make the
@@ -166,3 +171,32 @@ def dequant_matmul_fp32(x, weight_int8, scale, bias=None):
     if bias is not None:
         y = y + np.asarray(bias).astype(np.float32)
     return y.reshape(x.shape[:-1] + (w.shape[0],))
+
+
+def rmsnorm_torch(x, weight, eps: float = 1e-6):
+    """The reference's CPU RMSNorm (normalization.py:32-45): in fp32,
+    ``rms = 1 / sqrt(mean(x^2) + eps)``; ``(x * rms)`` rounded to ``x.dtype``,
+    then times ``weight`` with the usual dtype promotion."""
+    x = np.asarray(x)
+    x32 = x.astype(np.float32)
+    rms = (np.float32(1.0) / np.sqrt((x32 * x32).mean(axis=-1, keepdims=True, dtype=np.float32) + np.float32(eps)))
+    return (x32 * rms).astype(x.dtype) * np.asarray(weight)
+
+
+def swiglu_torch(gate, up):
+    """The reference's CPU SwiGLU (activations.py:36-46): ``silu(gate) * up``;
+    for fp16 tensors ``silu`` is computed in fp32 and rounded to fp16, then
+    the product is rounded to fp16."""
+    gate = np.asarray(gate)
+    g32 = gate.astype(np.float32)
+    silu = (g32 / (np.float32(1.0) + np.exp(-g32))).astype(gate.dtype)
+    return silu * np.asarray(up)
+
+
+def swiglu_mlp(x, norm_weight, eps, wg, sg, wu, su, wd, sd):
+    """RMSNorm -> gate / up W8A16 GEMMs -> SwiGLU -> down W8A16 GEMM, each
+    step with the reference's CPU arithmetic."""
+    xn = rmsnorm_torch(x, norm_weight, eps)
+    gate = int8_gemm_torch(xn, wg, sg)
+    up = int8_gemm_torch(xn, wu, su)
+    return int8_gemm_torch(swiglu_torch(gate, up), wd, sd)

@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = (
     "rla_gather_columns", "rla_launch_count", "rla_get_device_error", "rla_last_error", "rla_version",
     "rla_set_decode_kernel", "rla_w8a16_gemm_allgather", "rla_set_peer_wait_limit", "rla_peer_alloc",
     "rla_peer_free", "rla_ipc_export", "rla_ipc_open", "rla_ipc_close",
+    "rla_w8a16_gemm_swiglu", "rla_w8a16_swiglu_workspace_size", "rla_rmsnorm",
 )
 
 MAX_PEERS = 8
@@ -93,6 +94,13 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.rla_ipc_open.restype = ctypes.c_int
         lib.rla_ipc_close.argtypes = [p]
         lib.rla_ipc_close.restype = ctypes.c_int
+        lib.rla_w8a16_gemm_swiglu.argtypes = [p, i64, p, p, i64, p, p, ctypes.c_int, p, p, ctypes.c_int, p, i64,
+                                              i64, i64, i64, p, sz, p]
+        lib.rla_w8a16_gemm_swiglu.restype = ctypes.c_int
+        lib.rla_w8a16_swiglu_workspace_size.argtypes = [i64, i64, i64]
+        lib.rla_w8a16_swiglu_workspace_size.restype = sz
+        lib.rla_rmsnorm.argtypes = [p, i64, p, ctypes.c_int, ctypes.c_float, p, i64, i64, i64, p]
+        lib.rla_rmsnorm.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -172,6 +180,59 @@ def w8a16_gemm(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor
             bias.data_ptr() if bias is not None else None, _bias_dtype(bias),
             out.data_ptr(), out.stride(0) if M > 0 else N, M, N, K, ws_ptr, ws_bytes, stream)
     _check(st, "rla_w8a16_gemm")
+    return out
+
+
+def w8a16_gemm_swiglu(x2d: torch.Tensor, w_gate: torch.Tensor, scale_gate: torch.Tensor, w_up: torch.Tensor,
+                      scale_up: torch.Tensor, bias_gate=None, bias_up=None,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """``y[M, N] = fp16(silu(g) * u)`` with ``g``, ``u`` the fp16 outputs of
+    the gate and up W8A16 GEMMs, in one launch (``rla_w8a16_gemm_swiglu``).
+    ``w_gate``/``w_up`` int8 ``[N, K]`` with the same row stride; scales
+    (and biases) of one dtype."""
+    lib = load_library()
+    M, K = x2d.shape
+    N = w_gate.shape[0]
+    if w_up.shape != w_gate.shape or w_up.stride() != w_gate.stride():
+        raise ValueError("w_gate and w_up must have the same shape and strides")
+    if scale_up.dtype != scale_gate.dtype:
+        raise TypeError("scale_gate and scale_up must have the same dtype")
+    if (bias_gate is None) != (bias_up is None) or (bias_gate is not None and bias_gate.dtype != bias_up.dtype):
+        raise TypeError("bias_gate and bias_up must both be given (same dtype) or both be None")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=x2d.device)
+    stream = torch.cuda.current_stream(x2d.device).cuda_stream
+    need = lib.rla_w8a16_swiglu_workspace_size(M, N, K)
+    ws_ptr, ws_bytes = None, 0
+    if need:
+        ws = _workspace(x2d.device, stream, need)
+        ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(x2d.device):
+        st = lib.rla_w8a16_gemm_swiglu(
+            x2d.data_ptr(), x2d.stride(0) if M > 0 else K, w_gate.data_ptr(), w_up.data_ptr(),
+            w_gate.stride(0) if N > 0 else K, scale_gate.data_ptr(), scale_up.data_ptr(), _scale_dtype(scale_gate),
+            bias_gate.data_ptr() if bias_gate is not None else None,
+            bias_up.data_ptr() if bias_up is not None else None, _bias_dtype(bias_gate),
+            out.data_ptr(), out.stride(0) if M > 0 else N, M, N, K, ws_ptr, ws_bytes, stream)
+    _check(st, "rla_w8a16_gemm_swiglu")
+    return out
+
+
+def rmsnorm(x2d: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 rows: ``fp16(x * rsqrt(mean(x^2) + eps) * weight)`` (``rla_rmsnorm``)."""
+    lib = load_library()
+    dt = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}.get(weight.dtype)
+    if dt is None:
+        raise TypeError(f"rmsnorm: unsupported weight dtype {weight.dtype}")
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    M, K = x2d.shape
+    if out is None:
+        out = torch.empty((M, K), dtype=torch.float16, device=x2d.device)
+    stream = torch.cuda.current_stream(x2d.device).cuda_stream
+    with torch.cuda.device(x2d.device):
+        st = lib.rla_rmsnorm(x2d.data_ptr(), x2d.stride(0) if M > 0 else K, w.data_ptr(), dt, float(eps),
+                             out.data_ptr(), out.stride(0) if M > 0 else K, M, K, stream)
+    _check(st, "rla_rmsnorm")
     return out
 
 

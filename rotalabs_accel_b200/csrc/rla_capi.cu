@@ -138,6 +138,25 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
   return p;
 }
 
+// The gated (SwiGLU) GEMM: gate and up of N outputs are 2N weight rows.
+// Decode: the skinny kernel (its shape for 2N rows; never the stream
+// kernel), prefill: the tcgen05 kernel with 64-output tiles, else generic.
+Plan make_plan_gated(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace) {
+  Plan p;
+  if (M == 0 || N == 0) return p;
+  if (K == 0 || !aligned || K % 16 != 0) {
+    p.kernel = RLA_KERNEL_GENERIC;
+    return p;
+  }
+  if (M <= 32) {
+    skinny_shape(p, M, 2 * N, K, have_workspace, device_sm_count());
+    return p;
+  }
+  p = make_plan(M, 2 * N, K, aligned, have_workspace);  // the tcgen05 plan for 2N rows: 64-output tiles
+  p.grid_x = static_cast<int>((N + 63) / 64);
+  return p;
+}
+
 }  // namespace rla
 
 using namespace rla;
@@ -256,6 +275,75 @@ int rla_quantize_per_channel(const void* w, int w_dtype, int64_t ldw, int64_t N,
   cudaError_t e = launch_quantize(w, w_dtype, ldw, N, K, q, ldq, scale, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     set_error("rla_quantize_per_channel: %s", cudaGetErrorString(e));
+    return RLA_ERR_CUDA;
+  }
+  note_launch();
+  return RLA_OK;
+}
+
+size_t rla_w8a16_swiglu_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N < 0 || K < 0) return 0;
+  return make_plan_gated(M, N, K, true, true).workspace;
+}
+
+int rla_w8a16_gemm_swiglu(const void* x, int64_t ldx, const int8_t* w_gate, const int8_t* w_up, int64_t ldw,
+                          const void* scale_gate, const void* scale_up, int scale_dtype, const void* bias_gate,
+                          const void* bias_up, int bias_dtype, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm_swiglu: M, N, K must be in [0, 2^31)");
+  if (M == 0 || N == 0) return RLA_OK;
+  if (scale_dtype != RLA_DTYPE_F16 && scale_dtype != RLA_DTYPE_F32)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm_swiglu: scale_dtype must be F16 or F32");
+  if (bias_dtype != RLA_DTYPE_NONE && bias_dtype != RLA_DTYPE_F16 && bias_dtype != RLA_DTYPE_F32)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm_swiglu: bias_dtype must be NONE, F16 or F32");
+  if (bias_dtype != RLA_DTYPE_NONE && (!bias_gate || !bias_up))
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm_swiglu: bias_dtype set but a bias is NULL");
+  if (!y || !scale_gate || !scale_up || (K > 0 && (!x || !w_gate || !w_up)))
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm_swiglu: null x, weight, scale or y");
+  if (ldy < N || (K > 0 && (ldx < K || ldw < K)))
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_w8a16_gemm_swiglu: leading dimensions must be >= the row length");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(RLA_ERR_WORKSPACE, "rla_w8a16_gemm_swiglu: workspace must be 256-byte aligned");
+  GemmArgs a{x, ldx, w_gate, ldw, scale_gate, scale_dtype == RLA_DTYPE_F32 ? 1 : 0, bias_gate,
+             bias_dtype == RLA_DTYPE_NONE ? 0 : bias_dtype == RLA_DTYPE_F16 ? 1 : 2,
+             y, ldy, (int)M, (int)N, (int)K};
+  a.w_up = w_up;
+  a.scale_up = scale_up;
+  a.bias_up = bias_up;
+  const bool aligned = aligned16(x) && aligned16(w_gate) && aligned16(w_up) && (ldx % 8 == 0) && (ldw % 16 == 0);
+  Plan p = make_plan_gated(M, N, K, aligned, workspace != nullptr && workspace_bytes > 0);
+  if (p.workspace > workspace_bytes) p = make_plan_gated(M, N, K, aligned, false);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  switch (p.kernel) {
+    case RLA_KERNEL_SKINNY: e = launch_skinny(a, p, workspace, s); break;
+    case RLA_KERNEL_TCGEN05: e = launch_tcgen05(a, p, s); break;
+    case RLA_KERNEL_GENERIC: e = launch_generic(a, s); break;
+    default: return fail(RLA_ERR_UNSUPPORTED, "rla_w8a16_gemm_swiglu: no kernel for this shape");
+  }
+  if (e != cudaSuccess) {
+    set_error("rla_w8a16_gemm_swiglu: launch of kernel family %d failed: %s", p.kernel, cudaGetErrorString(e));
+    return RLA_ERR_CUDA;
+  }
+  note_launch();
+  return RLA_OK;
+}
+
+int rla_rmsnorm(const void* x, int64_t ldx, const void* weight, int weight_dtype, float eps, void* y, int64_t ldy,
+                int64_t M, int64_t K, void* stream) {
+  if (M < 0 || K < 0 || M > INT32_MAX || K > INT32_MAX)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_rmsnorm: M, K must be in [0, 2^31)");
+  if (M == 0 || K == 0) return RLA_OK;
+  if (!x || !weight || !y) return fail(RLA_ERR_INVALID_ARGUMENT, "rla_rmsnorm: null pointer");
+  if (weight_dtype != RLA_DTYPE_F32 && weight_dtype != RLA_DTYPE_F16 && weight_dtype != RLA_DTYPE_BF16)
+    return fail(RLA_ERR_INVALID_ARGUMENT, "rla_rmsnorm: weight_dtype must be F32, F16 or BF16");
+  if (ldx < K || ldy < K) return fail(RLA_ERR_INVALID_ARGUMENT, "rla_rmsnorm: leading dimensions must be >= K");
+  if (!(eps >= 0.f)) return fail(RLA_ERR_INVALID_ARGUMENT, "rla_rmsnorm: eps must be >= 0");
+  const cudaError_t e = launch_rmsnorm(x, ldx, weight, weight_dtype, eps, y, ldy, (int)M, (int)K,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("rla_rmsnorm: %s", cudaGetErrorString(e));
     return RLA_ERR_CUDA;
   }
   note_launch();

@@ -62,6 +62,15 @@ RLA_DEVFN void rla_i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
   asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(bias));
 }
 
+// SwiGLU of one output: fp16(silu(g) * u), silu(g) = g * sigmoid(g) =
+// g / (1 + e^-g), in fp32, from gate and up values already rounded to fp16
+// (the rounding points of a gate GEMM, an up GEMM and a separate SwiGLU pass).
+RLA_DEVFN __half rla_swiglu(float gate, float up) {
+  const float g = __half2float(__float2half_rn(gate));
+  const float u = __half2float(__float2half_rn(up));
+  return __float2half_rn(g / (1.0f + __expf(-g)) * u);
+}
+
 // ---------------------------------------------------------------------------
 // Global loads
 // ---------------------------------------------------------------------------

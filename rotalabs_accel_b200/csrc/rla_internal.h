@@ -48,6 +48,12 @@ struct GemmArgs {
   // world == 0 unless the call is rla_w8a16_gemm_allgather; then y is the
   // full [M, world * n_local] output and N = n_local.
   PeerOut peer{};
+  // Gated (SwiGLU) GEMM, rla_w8a16_gemm_swiglu: w / scale / bias are the gate
+  // projection, these the up projection (same layout), and
+  // y = fp16(silu(gate) * up) with gate and up rounded to fp16 first.
+  const int8_t* w_up = nullptr;
+  const void* scale_up = nullptr;
+  const void* bias_up = nullptr;
 };
 
 // A launch plan chosen by the per-shape selector.
@@ -84,7 +90,9 @@ cudaError_t launch_stream(const GemmArgs& a, const Plan& p, void* workspace, cud
 size_t stream_workspace_bytes(int64_t M, int ctas);
 size_t stream_smem_bytes(int nt);
 cudaError_t launch_tcgen05(const GemmArgs& a, const Plan& p, cudaStream_t s);
-cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s);
+cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s);  // also the gated form (a.w_up set)
+cudaError_t launch_rmsnorm(const void* x, int64_t ldx, const void* weight, int weight_dtype, float eps, void* y,
+                           int64_t ldy, int M, int K, cudaStream_t s);
 cudaError_t launch_fill(const GemmArgs& a, cudaStream_t s);
 
 size_t tcgen05_smem_bytes(int bm, int stages);

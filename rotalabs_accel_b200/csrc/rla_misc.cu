@@ -20,40 +20,59 @@ __device__ __forceinline__ float load_bias(const void* p, int kind, int n) {
 // (output channel n, block of 8 tokens); lanes stride over k, fp32
 // accumulation, warp-shuffle reduction.  Used only for shapes the fast
 // kernels' 16-byte vector / TMA rules exclude (ragged K, odd strides).
+// Gated form (GLU): the warp also accumulates the up projection's row n and
+// writes fp16(silu(gate) * up).
 // ---------------------------------------------------------------------------
+template <bool GLU>
 __global__ void w8a16_generic_kernel(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w,
                                      int64_t ldw, const void* __restrict__ scale, int scale_f32,
                                      const void* __restrict__ bias, int bias_kind, __half* __restrict__ y,
-                                     int64_t ldy, int M, int N, int K) {
+                                     int64_t ldy, int M, int N, int K, const int8_t* __restrict__ w_up,
+                                     const void* __restrict__ scale_up, const void* __restrict__ bias_up) {
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t mblocks = (M + 7) / 8;
   if (gw >= mblocks * N) return;
   const int n = static_cast<int>(gw % N);
   const int mb = static_cast<int>(gw / N);
-  float acc[8];
+  float acc[8], accu[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  for (int j = 0; j < 8; ++j) acc[j] = accu[j] = 0.f;
   const int8_t* wr = w + static_cast<int64_t>(n) * ldw;
+  const int8_t* wu = GLU ? w_up + static_cast<int64_t>(n) * ldw : nullptr;
   for (int k = lane; k < K; k += 32) {
     const float wv = static_cast<float>(wr[k]);
+    const float uv = GLU ? static_cast<float>(wu[k]) : 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int m = mb * 8 + j;
-      if (m < M) acc[j] = fmaf(__half2float(x[static_cast<int64_t>(m) * ldx + k]), wv, acc[j]);
+      if (m < M) {
+        const float xv = __half2float(x[static_cast<int64_t>(m) * ldx + k]);
+        acc[j] = fmaf(xv, wv, acc[j]);
+        if (GLU) accu[j] = fmaf(xv, uv, accu[j]);
+      }
     }
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    for (int o = 16; o > 0; o >>= 1) {
+      acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+      if (GLU) accu[j] += __shfl_xor_sync(0xffffffffu, accu[j], o);
+    }
   if (lane == 0) {
     const float sc = load_scale(scale, scale_f32, n);
     const float bi = load_bias(bias, bias_kind, n);
+    const float scu = GLU ? load_scale(scale_up, scale_f32, n) : 0.f;
+    const float biu = GLU ? load_bias(bias_up, bias_kind, n) : 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int m = mb * 8 + j;
-      if (m < M) y[static_cast<int64_t>(m) * ldy + n] = __float2half_rn(fmaf(acc[j], sc, bi));
+      if (m >= M) continue;
+      if (GLU)
+        y[static_cast<int64_t>(m) * ldy + n] = rla_swiglu(fmaf(acc[j], sc, bi), fmaf(accu[j], scu, biu));
+      else
+        y[static_cast<int64_t>(m) * ldy + n] = __float2half_rn(fmaf(acc[j], sc, bi));
     }
   }
 }
@@ -62,9 +81,88 @@ cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s) {
   const int64_t warps = (int64_t)((a.M + 7) / 8) * a.N;
   const int64_t blocks = (warps * 32 + 255) / 256;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  w8a16_generic_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __half*>(a.x), a.ldx, a.w, a.ldw,
-                                                        a.scale, a.scale_f32, a.bias, a.bias_kind,
-                                                        static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K);
+  auto kern = a.w_up ? w8a16_generic_kernel<true> : w8a16_generic_kernel<false>;
+  kern<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __half*>(a.x), a.ldx, a.w, a.ldw, a.scale, a.scale_f32,
+                                        a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K,
+                                        a.w_up, a.scale_up, a.bias_up);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm of fp16 rows, the arithmetic of rotalabs-accel's CUDA RMSNorm
+// (kernels/normalization.py:66-101): per row, the mean of x^2 in fp32,
+// rrms = rsqrt(mean + eps), y = fp16(x * rrms * w) computed in fp32.  One CTA
+// per row; 16-byte loads when the row is aligned.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float load_weight(const void* w, int dtype, int k) {
+  return dtype == RLA_DTYPE_F32  ? static_cast<const float*>(w)[k]
+         : dtype == RLA_DTYPE_F16 ? __half2float(static_cast<const __half*>(w)[k])
+                                  : __bfloat162float(static_cast<const __nv_bfloat16*>(w)[k]);
+}
+
+__global__ void rmsnorm_rows_kernel(const __half* __restrict__ x, int64_t ldx, const void* __restrict__ weight,
+                                    int weight_dtype, float eps, __half* __restrict__ y, int64_t ldy, int K,
+                                    int vec) {
+  const __half* xr = x + static_cast<int64_t>(blockIdx.x) * ldx;
+  __half* yr = y + static_cast<int64_t>(blockIdx.x) * ldy;
+  float ss = 0.f;
+  if (vec) {
+    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+  } else {
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      const float f = __half2float(xr[k]);
+      ss = fmaf(f, f, ss);
+    }
+  }
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float rrms = rsqrtf(red[0] / static_cast<float>(K) + eps);
+  if (vec) {
+    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+      uint4 o;
+      __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        oh[i] = __floats2half2_rn(f.x * rrms * load_weight(weight, weight_dtype, k + 2 * i),
+                                  f.y * rrms * load_weight(weight, weight_dtype, k + 2 * i + 1));
+      }
+      *reinterpret_cast<uint4*>(yr + k) = o;
+    }
+  } else {
+    for (int k = threadIdx.x; k < K; k += blockDim.x)
+      yr[k] = __float2half_rn(__half2float(xr[k]) * rrms * load_weight(weight, weight_dtype, k));
+  }
+}
+
+cudaError_t launch_rmsnorm(const void* x, int64_t ldx, const void* weight, int weight_dtype, float eps, void* y,
+                           int64_t ldy, int M, int K, cudaStream_t s) {
+  const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+  const int threads = K >= 4096 ? 512 : 256;
+  rmsnorm_rows_kernel<<<(unsigned)M, threads, 0, s>>>(static_cast<const __half*>(x), ldx, weight, weight_dtype, eps,
+                                                     static_cast<__half*>(y), ldy, K, vec ? 1 : 0);
   return cudaGetLastError();
 }
 

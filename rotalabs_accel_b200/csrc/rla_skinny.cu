@@ -26,6 +26,11 @@
 // weight bytes while the previous kernel in the stream finishes, and reads
 // nothing before that kernel is done (rla_griddep_wait).
 //
+// Gated form (GLU, rla_w8a16_gemm_swiglu): a warp's 16 MMA rows are 8 gate
+// rows (A rows 0-7) and the same 8 rows of the up projection (A rows 8-15),
+// so one lane holds gate and up of the same output and the epilogue computes
+// fp16(silu(gate) * up) in registers; a CTA covers 8 * WN outputs.
+//
 // With a peer exchange (PEER, rla_w8a16_gemm_allgather) the epilogue stores
 // pairs of rows into y and, as flagged words, into every peer's receive
 // buffer, and every CTA ends with peer_finish (rla_peer.cuh).
@@ -40,14 +45,16 @@ struct XFrag {
   uint4 v[NT][2];
 };
 
-template <int NT, int WN, int WK, int U, bool PEER>
+template <int NT, int WN, int WK, int U, bool PEER, bool GLU>
 __global__ void __launch_bounds__(32 * WN * WK)
     w8a16_skinny_kernel(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,
                         const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias,
                         int bias_kind, __half* __restrict__ y, int64_t ldy, int M, int N, int K,
                         int chunks_per_split, float* __restrict__ partial, unsigned int* __restrict__ counters,
-                        const __grid_constant__ PeerOut po) {
-  constexpr int ROWS = 16 * WN;
+                        const __grid_constant__ PeerOut po, const int8_t* __restrict__ w_up,
+                        const void* __restrict__ scale_up, const void* __restrict__ bias_up) {
+  static_assert(!(PEER && GLU), "the gated form has no peer exchange");
+  constexpr int OUTS = GLU ? 8 * WN : 16 * WN;  // output channels per CTA
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int wn = warp % WN;
@@ -55,12 +62,12 @@ __global__ void __launch_bounds__(32 * WN * WK)
   const int g = lane >> 2;
   const int q = lane & 3;
 
-  const int row_base = blockIdx.x * ROWS;
-  const int n0 = row_base + wn * 16;
+  const int row_base = blockIdx.x * OUTS;
+  const int n0 = row_base + wn * (GLU ? 8 : 16);
   const int r0 = min(n0 + g, N - 1);
-  const int r1 = min(n0 + g + 8, N - 1);
+  const int r1 = GLU ? r0 : min(n0 + g + 8, N - 1);
   const int8_t* wrow0 = w + (int64_t)r0 * ldw + q * 16;
-  const int8_t* wrow1 = w + (int64_t)r1 * ldw + q * 16;
+  const int8_t* wrow1 = (GLU ? w_up : w) + (int64_t)r1 * ldw + q * 16;
 
   bool xrow_ok[NT];
   const __half* xrow[NT];
@@ -156,7 +163,31 @@ __global__ void __launch_bounds__(32 * WN * WK)
   }
 
   // Accumulator element (t, i): row n = n0 + g + 8*(i>>1), token m = 8t + 2q + (i&1).
+  // Gated form: i>>1 = 0 is the gate, 1 the up projection of output n0 + g.
   if (gridDim.y == 1) {
+    if constexpr (GLU) {
+      const int n = n0 + g;
+      if (wk == 0 && n < N) {
+        const float scg = scale_f32 ? static_cast<const float*>(scale)[n]
+                                    : __half2float(static_cast<const __half*>(scale)[n]);
+        const float scu = scale_f32 ? static_cast<const float*>(scale_up)[n]
+                                    : __half2float(static_cast<const __half*>(scale_up)[n]);
+        const float big = bias_kind == 0 ? 0.f
+                          : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias)[n])
+                                           : static_cast<const float*>(bias)[n];
+        const float biu = bias_kind == 0 ? 0.f
+                          : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias_up)[n])
+                                           : static_cast<const float*>(bias_up)[n];
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = t * 8 + 2 * q + j;
+            if (m < M) y[(int64_t)m * ldy + n] = rla_swiglu(fmaf(acc[t][j], scg, big), fmaf(acc[t][2 + j], scu, biu));
+          }
+      }
+      return;
+    }
     if (wk == 0) {
 #pragma unroll
       for (int hi = 0; hi < 2; ++hi) {
@@ -189,18 +220,22 @@ __global__ void __launch_bounds__(32 * WN * WK)
   }
 
   // ---- split-K across CTAs: publish this slice, the last CTA adds them all ----
+  // Partial sums [splits][M][NP]; the gated form keeps gate in columns
+  // [0, N) and up in [N, 2N).
+  constexpr int NPF = GLU ? 2 : 1;
   if (wk == 0) {
-    float* part = partial + (int64_t)blockIdx.y * M * N;
+    float* part = partial + (int64_t)blockIdx.y * M * N * NPF;
 #pragma unroll
     for (int hi = 0; hi < 2; ++hi) {
-      const int n = n0 + g + 8 * hi;
+      const int n = GLU ? n0 + g : n0 + g + 8 * hi;
       if (n >= N) continue;
+      const int col = GLU ? hi * N + n : n;
 #pragma unroll
       for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int m = t * 8 + 2 * q + j;
-          if (m < M) __stcg(part + (int64_t)m * N + n, acc[t][2 * hi + j]);
+          if (m < M) __stcg(part + (int64_t)m * N * NPF + col, acc[t][2 * hi + j]);
         }
     }
   }
@@ -218,7 +253,32 @@ __global__ void __launch_bounds__(32 * WN * WK)
   }
   __threadfence();
 
-  const int rows_here = min(ROWS, N - row_base);
+  const int rows_here = min(OUTS, N - row_base);
+  if constexpr (GLU) {
+    for (int idx = threadIdx.x; idx < rows_here * M; idx += blockDim.x) {
+      const int n = row_base + idx % rows_here;
+      const int m = idx / rows_here;
+      float sg = 0.f, su = 0.f;
+      for (int sidx = 0; sidx < (int)gridDim.y; ++sidx) {
+        const float* row = partial + ((int64_t)sidx * M + m) * 2 * N;
+        sg += __ldcg(row + n);
+        su += __ldcg(row + N + n);
+      }
+      const float scg =
+          scale_f32 ? static_cast<const float*>(scale)[n] : __half2float(static_cast<const __half*>(scale)[n]);
+      const float scu =
+          scale_f32 ? static_cast<const float*>(scale_up)[n] : __half2float(static_cast<const __half*>(scale_up)[n]);
+      const float big = bias_kind == 0 ? 0.f
+                        : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias)[n])
+                                         : static_cast<const float*>(bias)[n];
+      const float biu = bias_kind == 0 ? 0.f
+                        : bias_kind == 1 ? __half2float(static_cast<const __half*>(bias_up)[n])
+                                         : static_cast<const float*>(bias_up)[n];
+      y[(int64_t)m * ldy + n] = rla_swiglu(fmaf(sg, scg, big), fmaf(su, scu, biu));
+    }
+    if (threadIdx.x == 0) counters[blockIdx.x] = 0u;  // leave the workspace re-usable
+    return;
+  }
   // Plain output: one element per step; exchange: one pair of rows per step.
   const int steps = PEER ? (M + 1) / 2 : M;
   for (int idx = threadIdx.x; idx < rows_here * steps; idx += blockDim.x) {
@@ -266,7 +326,9 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  auto kern = a.peer.world > 0 ? w8a16_skinny_kernel<NT, WN, WK, U, true> : w8a16_skinny_kernel<NT, WN, WK, U, false>;
+  auto kern = a.w_up ? w8a16_skinny_kernel<NT, WN, WK, U, false, true>
+              : a.peer.world > 0 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false>
+                                 : w8a16_skinny_kernel<NT, WN, WK, U, false, false>;
   PeerOut po = a.peer;
   if (po.world > 0) {
     // Unpacking CTAs: the whole grid when it is resident at once, else at
@@ -283,7 +345,7 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
   }
   return cudaLaunchKernelEx(&cfg, kern, static_cast<const __half*>(a.x), a.ldx, a.w,
                             a.ldw, a.scale, a.scale_f32, a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M,
-                            a.N, a.K, cps, partial, counters, po);
+                            a.N, a.K, cps, partial, counters, po, a.w_up, a.scale_up, a.bias_up);
 }
 
 // Instantiated configurations: NT in {1, 2, 4}; (WN, WK) in {(1, 8), (2, 4), (4, 2)}.

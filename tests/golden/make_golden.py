@@ -4,7 +4,8 @@ Run in a container where the reference is importable (its ``src/`` on
 ``PYTHONPATH``); the GPU box has no reference, so the outputs are committed
 as ``tests/golden/*.npz`` and only ever read there.
 
-    PYTHONPATH=<reference>/src python tests/golden/make_golden.py
+    PYTHONPATH=<reference>/src python tests/golden/make_golden.py          # everything
+    PYTHONPATH=<reference>/src python tests/golden/make_golden.py mlp      # ref_mlp.npz only
 
 Everything runs on the CPU, i.e. through the reference's own fallback:
 ``int8_gemm`` -> ``int8_gemm_torch`` (src/rotalabs_accel/kernels/gemm.py:234-238)
@@ -29,7 +30,47 @@ def _sha(t: torch.Tensor) -> str:
     return hashlib.sha256(t.contiguous().numpy().tobytes()).hexdigest()
 
 
+def mlp_vectors() -> None:
+    """Config 3 pieces through the reference's CPU path: rmsnorm_torch,
+    swiglu_torch and the composed block (RMSNorm -> Int8Linear gate and up
+    -> SwiGLU -> Int8Linear down), fp16 activations, fp16 RMSNorm weight."""
+    import rotalabs_accel as ra
+    from rotalabs_accel import int8_gemm, quantize_weight_per_channel, rmsnorm_torch, swiglu_torch
+    assert ra.__version__ == "0.2.0"
+    g = torch.Generator().manual_seed(33)
+    M, H, I = 8, 128, 352
+    x = torch.randn(M, H, generator=g).half()
+    x[3] = 0                                            # a zero row: rms = 1/sqrt(eps)
+    nw = (1 + 0.1 * torch.randn(H, generator=g)).half()
+    xn = rmsnorm_torch(x, nw, 1e-6)
+    qs = {}
+    for name, (n_out, n_in) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+        q, s = quantize_weight_per_channel(torch.randn(n_out, n_in, generator=g) * 0.02)
+        qs[name] = (q, s.half())
+    gate = int8_gemm(xn, *qs["gate"])
+    up = int8_gemm(xn, *qs["up"])
+    h = swiglu_torch(gate, up)
+    y = int8_gemm(h, *qs["down"])
+    # SwiGLU alone on a spread of magnitudes (large negative, zero, large positive)
+    ga = (torch.linspace(-30, 30, 241) * torch.rand(241, generator=g)).half()
+    ua = torch.randn(241, generator=g).half()
+    sa = swiglu_torch(ga, ua)
+    # RMSNorm alone with an fp32 weight (dtype promotion: fp32 result)
+    xr = (torch.randn(4, 96, generator=g) * 3).half()
+    wr = torch.rand(96, generator=g) + 0.5
+    yr = rmsnorm_torch(xr, wr, 1e-5)
+    np.savez_compressed(os.path.join(HERE, "ref_mlp.npz"), x=x.numpy(), norm_weight=nw.numpy(), eps=np.array(1e-6),
+                        xn=xn.numpy(), wg=qs["gate"][0].numpy(), sg=qs["gate"][1].numpy(),
+                        wu=qs["up"][0].numpy(), su=qs["up"][1].numpy(), wd=qs["down"][0].numpy(),
+                        sd=qs["down"][1].numpy(), gate=gate.numpy(), up=up.numpy(), h=h.numpy(), y=y.numpy(),
+                        swiglu_gate=ga.numpy(), swiglu_up=ua.numpy(), swiglu_out=sa.numpy(),
+                        rms_x=xr.numpy(), rms_w=wr.numpy(), rms_y=yr.numpy())
+    print("ref_mlp.npz written to", HERE)
+
+
 def main() -> None:
+    if len(sys.argv) > 1 and sys.argv[1] == "mlp":
+        return mlp_vectors()
     import rotalabs_accel as ra  # the reference package
     from rotalabs_accel import (int8_gemm, int8_gemm_torch, quantize_symmetric, dequantize,
                                 quantize_weight_per_channel, calculate_quantization_error,
@@ -131,6 +172,7 @@ def main() -> None:
                         scale=s16.numpy(), y=y.numpy(),
                         sha_x=np.array(_sha(x)), sha_w=np.array(_sha(q)),
                         ref_err=np.array(float((y.float() - ref32).abs().max())))
+    mlp_vectors()
     print("golden vectors written to", HERE)
 
 
