@@ -24,6 +24,10 @@ Reported (rank 0, one line):
              against the measured HBM copy bandwidth.
   prefill    (N=1) the M=2048 prefill GEMMs of the benchmark configuration,
              TFLOP/s, against the measured dense bf16/fp16 tensor peak.
+  mlp_block  (N=1) config 3, the Llama-2-7B MLP block (RMSNorm -> gated
+             gate/up GEMM -> down) at M=8 (TB/s; 3 launches, SwiGLU in the
+             decode kernel's epilogue) and M=2048 (TFLOP/s; 5 launches), next
+             to the same block unfused (6 launches).
   cpu_baseline  the CPU oracle (rotalabs-accel's CPU algorithm restated in
              numpy) on one pass of the sweep, on this host's cores.
 
@@ -200,6 +204,73 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def measure_mlp_block(ra, _capi, dev, capture, timed, peaks, args):
+    """Config 3: RMSNorm(4096) -> gate/up 4096 -> 11008 -> SwiGLU -> down
+    11008 -> 4096 at M = 8 (decode, HBM-bound: bytes / time) and M = 2048
+    (prefill, tensor-bound: GEMM FLOPs / time).  One CUDA graph per step of
+    the block as the package runs it (3 launches at M = 8, 5 at M = 2048), and of the unfused
+    composition through the same library (RMSNorm, gate GEMM, up GEMM, torch
+    SiLU and product, down GEMM: 6 launches) for comparison.  Each step uses one of 3 copies of
+    the weights (405 MB), more than L2."""
+    import torch
+    H, I, reps = 4096, 11008, 3
+    blocks = []
+    for r in range(reps):
+        g = torch.Generator(device=dev).manual_seed(3000 + r)
+        norm = ra.TritonRMSNorm(H).to(dev)
+        mlp = ra.Int8SwiGLU(H, I).to(dev)
+        mlp.quantize_weights(torch.randn(I, H, generator=g, device=dev) * 0.02,
+                             torch.randn(I, H, generator=g, device=dev) * 0.02,
+                             torch.randn(H, I, generator=g, device=dev) * 0.02)
+        for lin in (mlp.w_gate, mlp.w_up, mlp.w_down):
+            lin.scale = lin.scale.half()
+        blocks.append((norm, mlp))
+    out = {}
+    for M in (8, 2048):
+        xs = [torch.randn(M, H, device=dev).half() for _ in range(reps)]
+
+        def fused():
+            for (norm, mlp), x in zip(blocks, xs):
+                mlp(norm(x))
+
+        def unfused():
+            for (norm, mlp), x in zip(blocks, xs):
+                h = norm(x)
+                gate = ra.int8_gemm(h, mlp.w_gate.weight_int8, mlp.w_gate.scale)
+                up = ra.int8_gemm(h, mlp.w_up.weight_int8, mlp.w_up.scale)
+                ra.int8_gemm(torch.nn.functional.silu(gate) * up, mlp.w_down.weight_int8, mlp.w_down.scale)
+
+        steps = 2000 if M == 8 else 100
+        res = {}
+        for name, fn in (("fused", fused), ("unfused", unfused)):
+            gph = capture(fn)
+            ms, clk = timed(gph, steps, max(3, args.warmup // 4), sample_clocks=(name == "fused"))
+            res[name] = (ms / reps, clk)
+            del gph
+        us = res["fused"][0] * 1e3
+        wbytes = 3 * H * I
+        io = 2 * M * H * 2 + 2 * (2 * I + H)            # x in, y out, fp16 scales
+        entry = {"us_per_block": round(us, 2), "unfused_us_per_block": round(res["unfused"][0] * 1e3, 2),
+                 "launches_per_block": 3 if M <= 32 else 5, "unfused_launches_per_block": 6,
+                 "clocks": res["fused"][1]}
+        if M == 8:
+            tbs = (wbytes + io) / (us * 1e-6) / 1e12
+            entry.update({"value": round(tbs, 3), "unit": "TB/s",
+                          "roofline": {"bound": "hbm", "achieved": round(tbs * 1e3, 1), "peak": peaks["hbm_gbs"],
+                                       "unit": "GB/s", "frac": round(tbs * 1e3 / peaks["hbm_gbs"], 4),
+                                       "peak_kind": f"HBM copy ({peaks['source']})"}})
+        else:
+            tf = 3 * 2 * M * H * I / (us * 1e-6) / 1e12
+            entry.update({"value": round(tf, 1), "unit": "TFLOP/s",
+                          "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["bf16_tflops"],
+                                       "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4),
+                                       "peak_kind": f"dense bf16/fp16 burst ({peaks['source']})"}})
+        out[f"M={M}"] = entry
+    out["workload"] = ("BASELINE config 3: RMSNorm(4096) -> Int8Linear gate, up 4096->11008 -> SwiGLU -> "
+                       "Int8Linear down 11008->4096, random-init weights N(0, 0.02), x ~ N(0, 1) fp16")
+    return out
+
+
 def run_case(case: str) -> int:
     """Small fixed workloads for profiler captures (no timing):
     ``sweep`` the 16 decode GEMMs once each; ``decode`` 4 launches of
@@ -233,6 +304,12 @@ def run_case(case: str) -> int:
         x, q, s = prob(2048, 11008, 4096, 0)
         for _ in range(2):
             _capi.w8a16_gemm(x, q, s, None)
+    elif case in ("mlp8", "mlp2048"):
+        M = 8 if case == "mlp8" else 2048
+        x, qg, sg = prob(M, 11008, 4096, 0)
+        _, qu, su = prob(1, 11008, 4096, 1)
+        for _ in range(2):
+            _capi.w8a16_gemm_swiglu(x, qg, sg, qu, su)
     else:
         raise SystemExit(f"unknown case {case}")
     torch.cuda.synchronize()
@@ -252,7 +329,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
                     help="N > 1: output exchange of the column-parallel layers")
-    ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "prefill"),
+    ap.add_argument("--no-mlp", action="store_true", help="skip the config 3 MLP block measurement")
+    ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "prefill", "mlp8", "mlp2048"),
                     help="run one small fixed workload for a profiler capture and exit")
     args = ap.parse_args()
     if args.case:
@@ -459,6 +537,11 @@ def main():
                    "clocks": pclocks}
         del g_pre
 
+    # ---- config 3: the MLP block (N = 1) ----
+    mlp_block = None
+    if world == 1 and not args.no_mlp:
+        mlp_block = measure_mlp_block(ra, _capi, dev, capture, timed, peaks, args)
+
     # ---- CPU baseline (rank 0, N = 1) ----
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -502,6 +585,8 @@ def main():
         }
         if prefill:
             line["prefill"] = prefill
+        if mlp_block:
+            line["mlp_block"] = mlp_block
         if world > 1:
             line["gemm_only_ms_per_step"] = round(ms_gemm, 5)
         print(json.dumps(line), flush=True)

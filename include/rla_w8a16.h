@@ -246,10 +246,13 @@ RLA_API int rla_ipc_close(void* ptr);
  * computes silu(gate) * up in fp32 from the two fp16 outputs) with one
  * launch and no [M, N] intermediates.  w_gate and w_up are int8 [N, K] with
  * the same row stride ldw; scales [N] share scale_dtype, biases [N] share
- * bias_dtype (both NULL with RLA_DTYPE_NONE).  Workspace as rla_w8a16_gemm,
- * sized by rla_w8a16_swiglu_workspace_size.  Decode (M <= 32) runs the
- * skinny kernel with gate and up rows in one MMA tile, prefill the tcgen05
- * kernel with gate and up rows in one 128-lane TMEM tile.
+ * bias_dtype (both NULL with RLA_DTYPE_NONE).  Workspace sized by
+ * rla_w8a16_swiglu_workspace_size (same counter rules as rla_w8a16_gemm).
+ * Decode (M <= 32): one launch, the skinny kernel with gate and up rows in
+ * one MMA tile and the SwiGLU in its epilogue.  Prefill (M > 32): two
+ * tcgen05 GEMMs write fp16 gate and up into the workspace after its
+ * 4096-byte counter region (4096 + 4 * M * N bytes, rounded up; required:
+ * RLA_ERR_WORKSPACE otherwise), then one SwiGLU pass.
  */
 RLA_API int rla_w8a16_gemm_swiglu(const void* x, int64_t ldx, const int8_t* w_gate, const int8_t* w_up, int64_t ldw,
                                   const void* scale_gate, const void* scale_up, int scale_dtype, const void* bias_gate,

@@ -65,10 +65,12 @@ RLA_DEVFN void rla_i8x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
 // SwiGLU of one output: fp16(silu(g) * u), silu(g) = g * sigmoid(g) =
 // g / (1 + e^-g), in fp32, from gate and up values already rounded to fp16
 // (the rounding points of a gate GEMM, an up GEMM and a separate SwiGLU pass).
+// Fast-math intrinsics: their few-ulp fp32 error is far below the fp16
+// rounding that follows; for g <= -89, e^-g overflows to inf and the quotient
+// is the correct limit -0.
 RLA_DEVFN __half rla_swiglu(float gate, float up) {
-  const float g = __half2float(__float2half_rn(gate));
-  const float u = __half2float(__float2half_rn(up));
-  return __float2half_rn(g / (1.0f + __expf(-g)) * u);
+  const float2 gu = __half22float2(__floats2half2_rn(gate, up));
+  return __float2half_rn(__fdividef(gu.x, 1.0f + __expf(-gu.x)) * gu.y);
 }
 
 // ---------------------------------------------------------------------------

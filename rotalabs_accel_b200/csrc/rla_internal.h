@@ -48,9 +48,10 @@ struct GemmArgs {
   // world == 0 unless the call is rla_w8a16_gemm_allgather; then y is the
   // full [M, world * n_local] output and N = n_local.
   PeerOut peer{};
-  // Gated (SwiGLU) GEMM, rla_w8a16_gemm_swiglu: w / scale / bias are the gate
-  // projection, these the up projection (same layout), and
-  // y = fp16(silu(gate) * up) with gate and up rounded to fp16 first.
+  // Gated (SwiGLU) GEMM, rla_w8a16_gemm_swiglu, decode and generic kernels:
+  // w / scale / bias are the gate projection, these the up projection (same
+  // layout), and y = fp16(silu(gate) * up) with gate and up rounded to fp16
+  // first.
   const int8_t* w_up = nullptr;
   const void* scale_up = nullptr;
   const void* bias_up = nullptr;
@@ -91,6 +92,8 @@ size_t stream_workspace_bytes(int64_t M, int ctas);
 size_t stream_smem_bytes(int nt);
 cudaError_t launch_tcgen05(const GemmArgs& a, const Plan& p, cudaStream_t s);
 cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s);  // also the gated form (a.w_up set)
+cudaError_t launch_swiglu(const void* gate, const void* up, int64_t ld, void* y, int64_t ldy, int M, int N,
+                          cudaStream_t s);
 cudaError_t launch_rmsnorm(const void* x, int64_t ldx, const void* weight, int weight_dtype, float eps, void* y,
                            int64_t ldy, int M, int K, cudaStream_t s);
 cudaError_t launch_fill(const GemmArgs& a, cudaStream_t s);

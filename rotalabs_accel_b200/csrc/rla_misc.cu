@@ -3,6 +3,8 @@
 // assembly.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "rla_common.cuh"
 #include "rla_internal.h"
 
@@ -85,6 +87,48 @@ cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s) {
   kern<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __half*>(a.x), a.ldx, a.w, a.ldw, a.scale, a.scale_f32,
                                         a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K,
                                         a.w_up, a.scale_up, a.bias_up);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU of two fp16 [M, N] tensors: y = fp16(silu(gate) * up) in fp32.  The
+// prefill form of the gated GEMM (two tcgen05 GEMMs into the workspace, then
+// this pass): a streaming kernel at full occupancy hides the latency of the
+// exp / reciprocal that a GEMM epilogue with four warps cannot.
+// ---------------------------------------------------------------------------
+__global__ void swiglu_rows_kernel(const __half* __restrict__ gate, const __half* __restrict__ up, int64_t ld,
+                                   __half* __restrict__ y, int64_t ldy, int M, int N, int vec) {
+  const int64_t per_row = vec ? N / 8 : N;
+  const int64_t total = per_row * M;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / per_row;
+    const int64_t c = i - m * per_row;
+    if (vec) {
+      const uint4 g = *reinterpret_cast<const uint4*>(gate + m * ld + c * 8);
+      const uint4 u = *reinterpret_cast<const uint4*>(up + m * ld + c * 8);
+      const __half* gh = reinterpret_cast<const __half*>(&g);
+      const __half* uh = reinterpret_cast<const __half*>(&u);
+      uint4 o;
+      __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) oh[k] = rla_swiglu(__half2float(gh[k]), __half2float(uh[k]));
+      *reinterpret_cast<uint4*>(y + m * ldy + c * 8) = o;
+    } else {
+      y[m * ldy + c] = rla_swiglu(__half2float(gate[m * ld + c]), __half2float(up[m * ld + c]));
+    }
+  }
+}
+
+cudaError_t launch_swiglu(const void* gate, const void* up, int64_t ld, void* y, int64_t ldy, int M, int N,
+                          cudaStream_t s) {
+  const bool vec = N % 8 == 0 && ld % 8 == 0 && ldy % 8 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(up) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+  const int64_t work = (vec ? (int64_t)N / 8 : (int64_t)N) * M;
+  const int64_t blocks = std::min<int64_t>((work + 255) / 256, 148 * 16);
+  swiglu_rows_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(
+      static_cast<const __half*>(gate), static_cast<const __half*>(up), ld, static_cast<__half*>(y), ldy, M, N,
+      vec ? 1 : 0);
   return cudaGetLastError();
 }
 

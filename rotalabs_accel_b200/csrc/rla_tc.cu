@@ -26,14 +26,6 @@
 // No operand is ever converted into shared memory: shared-memory traffic is
 // the TMA writes, one read of the int8 tile and the MMA's read of x.
 //
-// Gated form (GLU, rla_w8a16_gemm_swiglu): a tile is 64 output channels; its
-// 128 TMEM lanes hold, in each 32-lane quarter q, 16 gate rows (lanes
-// 32q..32q+15, outputs 16q..16q+15) and the same 16 rows of the up
-// projection (lanes 32q+16..32q+31).  TMA brings the gate and up tiles
-// [64 x 64] into the two halves of the int8 stage; after the last k block a
-// gate thread takes its up partner's row with one warp shuffle and writes
-// fp16(silu(gate) * up).
-//
 // All waits are bounded (rla_mbar_wait); a timeout records a device error,
 // raises a CTA-wide abort flag and unwinds to the TMEM release.
 #include "rla_common.cuh"
@@ -69,12 +61,11 @@ __host__ __device__ constexpr int tmem_cols_for() {
   return (BM + tc::ASTAGES * 32) <= 256 ? 256 : 512;
 }
 
-template <int BM, int STAGES, bool GLU>
+template <int BM, int STAGES>
 __global__ void __launch_bounds__(tc::THREADS, 1)
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                    const __grid_constant__ CUtensorMap tmap_w_up, const void* __restrict__ scale, int scale_f32,
-                    const void* __restrict__ bias, int bias_kind, const void* __restrict__ scale_up,
-                    const void* __restrict__ bias_up, __half* __restrict__ y, int64_t ldy, int M, int N, int K) {
+                    const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias, int bias_kind,
+                    __half* __restrict__ y, int64_t ldy, int M, int N, int K) {
   using Smem = TcShared<BM, STAGES>;
   constexpr int TMEM_COLS = tmem_cols_for<BM>();
   constexpr uint32_t STAGE_TX = BM * 128 + tc::W_TILE_BYTES;
@@ -84,7 +75,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * (GLU ? tc::BN / 2 : tc::BN);  // first output channel of the tile
+  const int n0 = blockIdx.x * tc::BN;
   const int m0 = blockIdx.y * BM;
   const int num_kb = (K + tc::BK - 1) / tc::BK;
   volatile int* abort_flag = &sm.abort_flag;
@@ -105,7 +96,6 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
   if (warp == 0 && lane == 0) {
     rla_tma_prefetch_desc(&tmap_x);
     rla_tma_prefetch_desc(&tmap_w);
-    if constexpr (GLU) rla_tma_prefetch_desc(&tmap_w_up);
   }
   if (warp == 1) {
     rla_tmem_alloc(&sm.tmem_base, TMEM_COLS);
@@ -130,8 +120,6 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
         rla_mbar_arrive_expect_tx(&sm.full[s], STAGE_TX);
         rla_tma_load_2d(sm.x[s], &tmap_x, &sm.full[s], kb * tc::BK, m0);
         rla_tma_load_2d(sm.w[s], &tmap_w, &sm.full[s], kb * tc::BK, n0);
-        if constexpr (GLU)  // up rows into the second half of the int8 stage
-          rla_tma_load_2d(sm.w[s] + (tc::BN / 2) * tc::BK, &tmap_w_up, &sm.full[s], kb * tc::BK, n0);
         issued_until = kb + 1;
       }
       if (*abort_flag) {
@@ -171,11 +159,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
   } else {
     // ---------------- converters, then epilogue ----------------
     const int quarter = warp & 3;
-    // TMEM lane 32*quarter + lane holds weight row `row` of the int8 stage.
-    // Gated form: lanes 0-15 of a quarter are gate rows 16q.., lanes 16-31
-    // the up rows of the same outputs (second half of the stage).
-    const int row = GLU ? (lane < 16 ? quarter * 16 + lane : tc::BN / 2 + quarter * 16 + lane - 16)
-                        : quarter * 32 + lane;
+    const int row = quarter * 32 + lane;  // TMEM lane == weight row within the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int swz = (row >> 1) & 3;       // 64-byte swizzle of the int8 tile
     bool ok = true;
@@ -204,34 +188,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
       if (lane == 0) rla_mbar_arrive(&sm.afull[a]);
     }
     if (ok) ok = rla_mbar_wait(&sm.dfull, 0, RLA_DEVERR_TIMEOUT_ACCUM, abort_flag);
-    if (GLU && __all_sync(0xffffffffu, ok)) {
-      rla_tc_fence_after();
-      const int n = n0 + quarter * 16 + (lane & 15);
-      const bool is_gate = lane < 16;
-      float sc = 0.f, bi = 0.f;
-      if (n < N) {
-        const void* sp = is_gate ? scale : scale_up;
-        const void* bp = is_gate ? bias : bias_up;
-        sc = scale_f32 ? static_cast<const float*>(sp)[n] : __half2float(static_cast<const __half*>(sp)[n]);
-        bi = bias_kind == 0 ? 0.f
-             : bias_kind == 1 ? __half2float(static_cast<const __half*>(bp)[n])
-                              : static_cast<const float*>(bp)[n];
-      }
-#pragma unroll 1
-      for (int j = 0; j < BM / 32; ++j) {
-        if (m0 + j * 32 >= M) break;
-        uint32_t d[32];
-        rla_tmem_ld_32x32b_x32(tmem + lane_addr + j * 32, d);
-        rla_tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float mine = fmaf(__uint_as_float(d[i]), sc, bi);
-          const float up = __shfl_down_sync(0xffffffffu, mine, 16);  // lane l < 16 gets lane l + 16's
-          const int m = m0 + j * 32 + i;
-          if (is_gate && n < N && m < M) y[(int64_t)m * ldy + n] = rla_swiglu(mine, up);
-        }
-      }
-    } else if (!GLU && __all_sync(0xffffffffu, ok)) {
+    if (__all_sync(0xffffffffu, ok)) {
       rla_tc_fence_after();
       const int n = n0 + row;
       float sc = 0.f, bi = 0.f;
@@ -277,27 +234,21 @@ int tcgen05_tmem_cols(int bm) { return (bm + tc::ASTAGES * 32) <= 256 ? 256 : 51
 
 template <int BM, int STAGES>
 static cudaError_t launch_tc_cfg(const GemmArgs& a, const Plan& p, cudaStream_t s) {
-  const bool glu = a.w_up != nullptr;
-  const uint32_t wrows = glu ? tc::BN / 2 : tc::BN;  // weight rows per TMA box
-  CUtensorMap tx, tw, twu;
+  CUtensorMap tx, tw;
   if (!make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
                     (uint64_t)a.ldx * 2, tc::BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.ldw,
-                    tc::BK, wrows, CU_TENSOR_MAP_SWIZZLE_64B))
-    return cudaErrorInvalidValue;
-  twu = tw;
-  if (glu && !make_tmap_2d(&twu, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w_up, (uint64_t)a.K, (uint64_t)a.N,
-                           (uint64_t)a.ldw, tc::BK, wrows, CU_TENSOR_MAP_SWIZZLE_64B))
+                    tc::BK, tc::BN, CU_TENSOR_MAP_SWIZZLE_64B))
     return cudaErrorInvalidValue;
   const size_t smem = sizeof(TcShared<BM, STAGES>) + 1024;
-  auto kern = glu ? w8a16_tc_kernel<BM, STAGES, true> : w8a16_tc_kernel<BM, STAGES, false>;
+  auto kern = w8a16_tc_kernel<BM, STAGES>;
   // Per device and cheap: set on every launch rather than tracking devices.
   cudaError_t attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (attr_err != cudaSuccess) return attr_err;
   dim3 grid(p.grid_x, p.grid_y);
-  kern<<<grid, tc::THREADS, smem, s>>>(tx, tw, twu, a.scale, a.scale_f32, a.bias, a.bias_kind, a.scale_up,
-                                        a.bias_up, static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K);
+  kern<<<grid, tc::THREADS, smem, s>>>(tx, tw, a.scale, a.scale_f32, a.bias, a.bias_kind,
+                                        static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K);
   return cudaGetLastError();
 }
 

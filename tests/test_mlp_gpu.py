@@ -65,7 +65,10 @@ def test_gated_gemm_parity(cuda_lib, M, N, K, bias, sdt):
     n0 = _capi.launch_count()
     y = int8_gemm_swiglu(x, wg, sg, wu, su, bg, bu)
     torch.cuda.synchronize()
-    assert _capi.launch_count() == n0 + 1          # one native launch
+    # decode and ragged shapes: one fused launch; prefill: gate and up tcgen05
+    # GEMMs into the workspace, then the SwiGLU pass
+    prefill = M > 32 and K % 16 == 0
+    assert _capi.launch_count() == n0 + (3 if prefill else 1)
     assert y.shape == (M, N) and y.dtype == torch.float16
     _check(y, _ref_gated(x, wg, sg, wu, su, bg, bu), f"M={M} N={N} K={K}")
     # the same arithmetic as two of the library's GEMMs plus an fp32 SwiGLU
@@ -83,7 +86,8 @@ def test_gated_gemm_repeated_calls_share_workspace(cuda_lib):
     splits run back to back on one workspace."""
     from rotalabs_accel_b200 import _capi
     g = torch.Generator(device="cuda").manual_seed(5)
-    for (M, N, K) in [(16, 352, 4096), (8, 11008, 4096), (16, 256, 8192), (1, 352, 4096)] * 2:
+    # (a prefill call in between: its gate / up buffers share the workspace)
+    for (M, N, K) in [(16, 352, 4096), (8, 11008, 4096), (64, 352, 1024), (16, 256, 8192), (1, 352, 4096)] * 2:
         x = torch.randn(M, K, generator=g, device="cuda").half()
         wg, sg = _q(N, K, g)
         wu, su = _q(N, K, g)
@@ -135,7 +139,8 @@ def test_config3_block(cuda_lib, M):
     n0 = _capi.launch_count()
     y = mlp(norm(x))
     torch.cuda.synchronize()
-    assert _capi.launch_count() == n0 + 3           # rmsnorm, gate/up + SwiGLU, down
+    # rmsnorm, gate/up + SwiGLU (one launch in decode, three in prefill), down
+    assert _capi.launch_count() == n0 + (3 if M <= 32 else 5)
     assert y.shape == (M, 4096) and y.dtype == torch.float16
     _check(y, _ref_block(x, norm, mlp), f"config 3 block M={M}")
 
