@@ -136,7 +136,8 @@ cudaError_t launch_swiglu(const void* gate, const void* up, int64_t ld, void* y,
 // RMSNorm of fp16 rows, the arithmetic of rotalabs-accel's CUDA RMSNorm
 // (kernels/normalization.py:66-101): per row, the mean of x^2 in fp32,
 // rrms = rsqrt(mean + eps), y = fp16(x * rrms * w) computed in fp32.  One CTA
-// per row; 16-byte loads when the row is aligned.
+// per row; 16-byte loads when the row is aligned.  Launched with
+// programmatic dependent launch, so the next GEMM's prologue overlaps it.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float load_weight(const void* w, int dtype, int k) {
   return dtype == RLA_DTYPE_F32  ? static_cast<const float*>(w)[k]
@@ -147,6 +148,12 @@ __device__ __forceinline__ float load_weight(const void* w, int dtype, int k) {
 __global__ void rmsnorm_rows_kernel(const __half* __restrict__ x, int64_t ldx, const void* __restrict__ weight,
                                     int weight_dtype, float eps, __half* __restrict__ y, int64_t ldy, int K,
                                     int vec) {
+  // Programmatic dependent launch: the GEMM that follows (the MLP block's
+  // gate/up projection) may start now and stream its weights while this
+  // kernel runs; it reads y only after this grid completes.  Nothing is read
+  // or written here before the previous kernel in the stream has finished.
+  rla_griddep_launch_dependents();
+  rla_griddep_wait();
   const __half* xr = x + static_cast<int64_t>(blockIdx.x) * ldx;
   __half* yr = y + static_cast<int64_t>(blockIdx.x) * ldy;
   float ss = 0.f;
@@ -205,9 +212,17 @@ cudaError_t launch_rmsnorm(const void* x, int64_t ldx, const void* weight, int w
   const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
                    (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
   const int threads = K >= 4096 ? 512 : 256;
-  rmsnorm_rows_kernel<<<(unsigned)M, threads, 0, s>>>(static_cast<const __half*>(x), ldx, weight, weight_dtype, eps,
-                                                     static_cast<__half*>(y), ldy, K, vec ? 1 : 0);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)M);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rmsnorm_rows_kernel, static_cast<const __half*>(x), ldx, weight, weight_dtype, eps,
+                            static_cast<__half*>(y), ldy, K, vec ? 1 : 0);
 }
 
 // K == 0: the empty sum; y = bias (or 0).
