@@ -275,7 +275,10 @@ def run_case(case: str) -> int:
     """Small fixed workloads for profiler captures (no timing):
     ``sweep`` the 16 decode GEMMs once each; ``decode`` 4 launches of
     M=1, K=4096, N=14336; ``decode-large`` 3 launches of M=1, K=8192,
-    N=28672; ``prefill`` 2 launches of M=2048, K=4096, N=11008."""
+    N=28672; ``decode-large16`` 2 of M=16 on that shape; ``skinny16`` 3
+    launches of the skinny kernel at M=16, K=4096, N=14336; ``prefill`` 2
+    launches of M=2048, K=4096, N=11008; ``mlp8`` / ``mlp2048`` 2 gated
+    gate/up GEMMs of config 3."""
     import torch
     import rotalabs_accel_b200 as ra
     from rotalabs_accel_b200 import _capi
@@ -304,6 +307,16 @@ def run_case(case: str) -> int:
         x, q, s = prob(2048, 11008, 4096, 0)
         for _ in range(2):
             _capi.w8a16_gemm(x, q, s, None)
+    elif case == "decode-large16":
+        x, q, s = prob(16, 28672, 8192, 0)
+        for _ in range(2):
+            _capi.w8a16_gemm(x, q, s, None)
+    elif case == "skinny16":
+        _capi.set_decode_kernel("skinny")
+        x, q, s = prob(16, 14336, 4096, 0)
+        for _ in range(3):
+            _capi.w8a16_gemm(x, q, s, None)
+        _capi.set_decode_kernel("auto")
     elif case in ("mlp8", "mlp2048"):
         M = 8 if case == "mlp8" else 2048
         x, qg, sg = prob(M, 11008, 4096, 0)
@@ -330,7 +343,8 @@ def main():
     ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
                     help="N > 1: output exchange of the column-parallel layers")
     ap.add_argument("--no-mlp", action="store_true", help="skip the config 3 MLP block measurement")
-    ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "prefill", "mlp8", "mlp2048"),
+    ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "decode-large16", "skinny16", "prefill",
+                                       "mlp8", "mlp2048"),
                     help="run one small fixed workload for a profiler capture and exit")
     args = ap.parse_args()
     if args.case:
