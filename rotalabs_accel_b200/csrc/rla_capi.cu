@@ -130,7 +130,7 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
     }
     p.grid_x = static_cast<int>(ntiles);
     p.grid_y = static_cast<int>((M + p.bm - 1) / p.bm);
-    p.threads = 192;
+    p.threads = 320;
     p.smem = tcgen05_smem_bytes(p.bm, p.stages);
     return p;
   }

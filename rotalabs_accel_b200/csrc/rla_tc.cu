@@ -7,7 +7,7 @@
 // (N = BM), so D[n, m] lives in TMEM with one output channel per lane and the
 // per-channel scale is a single register per epilogue thread.
 //
-// Warp roles (192 threads, one CTA per SM):
+// Warp roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer: per 64-wide k block, one fp16 x tile
 //               [BM x 64] (128-byte swizzle, UMMA canonical K-major layout)
 //               and one int8 w tile [128 x 64] (64-byte swizzle) into a
@@ -16,13 +16,14 @@
 //               tcgen05.mma.kind::f16 (128 x BM x 16) per k block, A from
 //               TMEM, B from shared memory; tcgen05.commit frees the ring
 //               slot and the TMEM operand slot.
-//   warps 2-5   converters, then epilogue.  Thread i of warp w owns TMEM lane
-//               32*(w%4)+i = weight row i of the tile: it reads its 64 int8
-//               of the k block from shared memory (swizzle-aware, bank-
-//               conflict-free), converts to fp16 in registers and writes them
-//               with tcgen05.st into an A-operand slot of TMEM (ASTAGES
-//               slots).  After the last k block: tcgen05.ld of its row of D,
-//               x scale[n] (+ bias[n]), fp16, store.
+//   warps 2-9   converters, then epilogue, two per TMEM lane quarter.  Thread
+//               i of warp w owns TMEM lane 32*(w%4)+i = weight row i of the
+//               tile: it reads its half (32 int8) of the row's 64-byte k block
+//               from shared memory (swizzle-aware, bank-conflict-free),
+//               converts to fp16 in registers and writes them with tcgen05.st
+//               into its half of an A-operand slot of TMEM (ASTAGES slots).
+//               After the last k block: tcgen05.ld of every other 32-token
+//               block of its row of D, x scale[n] (+ bias[n]), fp16, store.
 // No operand is ever converted into shared memory: shared-memory traffic is
 // the TMA writes, one read of the int8 tile and the MMA's read of x.
 //
@@ -38,7 +39,8 @@ namespace tc {
 constexpr int BN = 128;          // weight rows per tile (MMA M, TMEM lanes)
 constexpr int BK = 64;           // k per pipeline stage
 constexpr int ASTAGES = 4;       // TMEM A-operand slots (32 columns each)
-constexpr int THREADS = 192;
+constexpr int CONVW = 8;         // converter (then epilogue) warps: 2 per TMEM lane quarter
+constexpr int THREADS = 64 + 32 * CONVW;
 constexpr int W_TILE_BYTES = BN * BK;  // int8
 }  // namespace tc
 
@@ -86,7 +88,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
       rla_mbar_init(&sm.empty[s], 1);
     }
     for (int a = 0; a < tc::ASTAGES; ++a) {
-      rla_mbar_init(&sm.afull[a], 4);  // one arrival per converter warp
+      rla_mbar_init(&sm.afull[a], tc::CONVW);  // one arrival per converter warp
       rla_mbar_init(&sm.aempty[a], 1);
     }
     rla_mbar_init(&sm.dfull, 1);
@@ -158,7 +160,11 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
     __syncwarp();
   } else {
     // ---------------- converters, then epilogue ----------------
+    // Warps 2 .. 2 + CONVW - 1: quarter = warp % 4 (the TMEM lanes a warp may
+    // touch), half = which 32 of the k block's 64 bytes it converts (and
+    // which 32-token column blocks it writes out in the epilogue).
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;  // TMEM lane == weight row within the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int swz = (row >> 1) & 3;       // 64-byte swizzle of the int8 tile
@@ -172,16 +178,17 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       rla_tc_fence_after();
       const uint8_t* wrow = sm.w[s] + row * 64;
-      uint32_t v[32];
+      uint32_t v[16];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * half + cc;      // 16-byte chunk of the row
         const uint4 q4 = *reinterpret_cast<const uint4*>(wrow + ((c ^ swz) << 4));
-        rla_i8x4_to_h2x2(q4.x, v[c * 8 + 0], v[c * 8 + 1]);
-        rla_i8x4_to_h2x2(q4.y, v[c * 8 + 2], v[c * 8 + 3]);
-        rla_i8x4_to_h2x2(q4.z, v[c * 8 + 4], v[c * 8 + 5]);
-        rla_i8x4_to_h2x2(q4.w, v[c * 8 + 6], v[c * 8 + 7]);
+        rla_i8x4_to_h2x2(q4.x, v[cc * 8 + 0], v[cc * 8 + 1]);
+        rla_i8x4_to_h2x2(q4.y, v[cc * 8 + 2], v[cc * 8 + 3]);
+        rla_i8x4_to_h2x2(q4.z, v[cc * 8 + 4], v[cc * 8 + 5]);
+        rla_i8x4_to_h2x2(q4.w, v[cc * 8 + 6], v[cc * 8 + 7]);
       }
-      rla_tmem_st_32x32b_x32(tmem + lane_addr + a_col0 + a * 32, v);
+      rla_tmem_st_32x32b_x16(tmem + lane_addr + a_col0 + a * 32 + half * 16, v);
       rla_tmem_wait_st();
       rla_tc_fence_before();
       __syncwarp();
@@ -199,7 +206,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
                               : static_cast<const float*>(bias)[n];
       }
 #pragma unroll 1
-      for (int j = 0; j < BM / 32; ++j) {
+      for (int j = half; j < BM / 32; j += 2) {
         if (m0 + j * 32 >= M) break;
         uint32_t d[32];
         rla_tmem_ld_32x32b_x32(tmem + lane_addr + j * 32, d);

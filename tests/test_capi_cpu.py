@@ -89,8 +89,10 @@ def test_selector_rules(lib):
     for K, N in ((4096, 12288), (4096, 11008), (11008, 4096)):
         p = _capi.plan(2048, N, K)
         assert p["kernel_name"] == "tcgen05" and p["w_rows"] == 128
-        assert p["grid_x"] * 128 >= N and p["grid_y"] * p["x_rows"] >= 2048
+        assert p["grid_x"] * 128 >= N and p["grid_y"] * p["x_rows"] >= 2048 and p["threads"] == 320
         assert p["smem"] <= 227 * 1024
+    p = _capi.plan(257, 384, 1040)
+    assert p["kernel_name"] == "tcgen05" and p["threads"] == 320 and p["grid_y"] * p["x_rows"] >= 257
     # the persistent stream-K decode kernel, when chosen: at most one CTA per SM
     _capi.set_decode_kernel("stream")
     try:

@@ -173,6 +173,7 @@ def test_llama70b_single_gpu(dev, M, KN):
     (1, 1, 16), (3, 33, 64), (7, 129, 80), (17, 100, 272), (31, 257, 1024),   # skinny, ragged
     (33, 130, 64), (64, 512, 4096), (100, 1000, 2048), (257, 384, 1040),     # tcgen05, ragged M/N/K
     (300, 129, 4100), (512, 256, 8),                                          # tcgen05, K % 16 != 0 / tiny K
+    (1000, 5000, 1040), (2304, 8200, 4096), (256, 18944, 64),                 # tcgen05, many tiles, ragged
     (5, 7, 13), (40, 50, 30), (2, 3, 1),                                      # generic (K % 8 != 0)
 ])
 @pytest.mark.parametrize("scale_dtype", [torch.float16, torch.float32])
