@@ -41,6 +41,16 @@ RLA_DEVFN uint64_t rla_globaltimer() {
 
 RLA_DEVFN void rla_record_error(unsigned int code) { atomicCAS(&rla_device_error, 0u, code); }
 
+// Split-K / stream-K arrival: one acquire-release atomic at gpu scope.  The
+// release publishes every store the caller's CTA made before its barrier
+// (cumulativity); the acquire makes the other CTAs' published stores visible
+// to the caller and, through the next CTA barrier, to its whole CTA.
+RLA_DEVFN unsigned int rla_arrive_acq_rel_gpu(unsigned int* counter) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+  return old;
+}
+
 // ---------------------------------------------------------------------------
 // int8 -> fp16, four values per 32-bit word.
 //

@@ -239,11 +239,10 @@ __global__ void __launch_bounds__(32 * WN * WK)
         }
     }
   }
-  __threadfence();
   __syncthreads();
   __shared__ int is_last;
   if (threadIdx.x == 0) {
-    const unsigned int prev = atomicAdd(counters + blockIdx.x, 1u);
+    const unsigned int prev = rla_arrive_acq_rel_gpu(counters + blockIdx.x);
     is_last = (prev == gridDim.y - 1);
   }
   __syncthreads();
@@ -251,7 +250,6 @@ __global__ void __launch_bounds__(32 * WN * WK)
     if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
     return;
   }
-  __threadfence();
 
   const int rows_here = min(OUTS, N - row_base);
   if constexpr (GLU) {

@@ -336,9 +336,8 @@ __global__ void __launch_bounds__(sk::THREADS, 1)
             }
         rla_named_bar_sync(2, NOUT * 32);       // every row group's piece is written
         if (cw == 0 && lane == 0) {
-          __threadfence();                      // release the CTA's pieces (cumulative)
-          *last_flag = atomicAdd(counters + p_first, 1u) == others ? 1 : 0;
-          __threadfence();
+          // releases the CTA's pieces, acquires the others'
+          *last_flag = rla_arrive_acq_rel_gpu(counters + p_first) == others ? 1 : 0;
         }
         rla_named_bar_sync(2, NOUT * 32);
         mode = *last_flag;
