@@ -39,14 +39,13 @@ int device_sm_count() {
 // Skinny kernel (M <= 32): the weight stream is the whole cost, so the plan
 // aims at enough independent 16-byte loads in flight on every SM
 // (Little's law: ~6.5 TB/s x ~1 us => several MB in flight machine-wide).
-// A CTA is 8 warps; rows per CTA and k-slicing are picked so there are at
-// least ~2 CTAs per SM, and split-K across CTAs is added only when the row
-// blocks alone cannot fill the machine (narrow N, e.g. a column shard).
+// A CTA is 8 warps; rows per CTA and k-slicing are picked by K, and split-K
+// across CTAs is added only while the whole grid stays resident (one wave).
 //
 // tcgen05 kernel (M > 32): tile 128 weight rows x BM tokens; BM = 256 for
 // long prefills, smaller for mid-size M so that the grid covers the SMs.
 // ---------------------------------------------------------------------------
-static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws, int sms) {
+static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws, int sms, bool gated = false) {
   p.kernel = RLA_KERNEL_SKINNY;
   p.nt = M <= 8 ? 1 : M <= 16 ? 2 : 4;
   const int64_t chunks = (K + 63) / 64;
@@ -61,11 +60,15 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   const int rows = 16 * p.wn;
   p.grid_x = static_cast<int>((N + rows - 1) / rows);
   p.splits = 1;
-  const int64_t target_ctas = 2LL * sms;
-  if (have_ws && p.grid_x < target_ctas && p.grid_x <= kMaxSplitRowBlocks) {
+  // Split K only as far as the whole grid stays resident at once (one wave):
+  // measured on B200, a second wave costs more than the extra parallelism
+  // gains (e.g. 4096 x 4096 at M = 16: 7.7 us unsplit vs 10.9 us with two
+  // slices at two resident CTAs per SM; at M = 1, four per SM, two slices win).
+  const int64_t resident = (int64_t)skinny_ctas_per_sm(p.nt, p.wn, p.wk, gated) * sms;
+  if (have_ws && p.grid_x < resident && p.grid_x <= kMaxSplitRowBlocks) {
     // Each CTA slice should still give every k-warp a few chunks.
     const int64_t max_splits = chunks / (2 * p.wk);
-    int64_t s = (target_ctas + p.grid_x - 1) / p.grid_x;
+    int64_t s = resident / p.grid_x;
     if (s > max_splits) s = max_splits;
     if (s > 32) s = 32;
     if (s > 1) p.splits = static_cast<int>(s);
@@ -154,7 +157,7 @@ Plan make_plan_gated(int64_t M, int64_t N, int64_t K, bool aligned, bool have_wo
     return p;
   }
   if (M <= 32) {
-    skinny_shape(p, M, 2 * N, K, have_workspace, device_sm_count());
+    skinny_shape(p, M, 2 * N, K, have_workspace, device_sm_count(), /*gated=*/true);
     return p;
   }
   p = make_plan(M, N, K, aligned, false);  // the tcgen05 plan of one projection

@@ -87,6 +87,9 @@ int device_sm_count();  // SMs of the current device (148 if it cannot be read)
 void set_error(const char* fmt, ...);
 
 cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
+// Resident CTAs per SM of the skinny kernel instance (plain or gated form);
+// 2 when the device cannot be queried.
+int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated);
 cudaError_t launch_stream(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
 size_t stream_workspace_bytes(int64_t M, int ctas);
 size_t stream_smem_bytes(int nt);

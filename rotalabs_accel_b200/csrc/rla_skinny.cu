@@ -357,6 +357,45 @@ static cudaError_t launch_nt(const GemmArgs& a, const Plan& p, void* ws, cudaStr
   return cudaErrorInvalidConfiguration;
 }
 
+template <int NT, int WN, int WK>
+static int ctas_per_sm_cfg(bool gated) {
+  constexpr int U = NT >= 4 ? 2 : 4;
+  static int cache[2] = {-1, -1};
+  int& c = cache[gated ? 1 : 0];
+  if (c < 0) {
+    int v = 0;
+    const cudaError_t e =
+        gated ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, w8a16_skinny_kernel<NT, WN, WK, U, false, true>,
+                                                              32 * WN * WK, 0)
+              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, w8a16_skinny_kernel<NT, WN, WK, U, false, false>,
+                                                              32 * WN * WK, 0);
+    if (e != cudaSuccess || v < 1) {
+      (void)cudaGetLastError();
+      return 2;   // no device to ask (e.g. planning on a CPU-only host)
+    }
+    c = v;
+  }
+  return c;
+}
+
+template <int NT>
+static int ctas_per_sm_nt(int wn, int wk, bool gated) {
+  if (wn == 1 && wk == 8) return ctas_per_sm_cfg<NT, 1, 8>(gated);
+  if (wn == 2 && wk == 4) return ctas_per_sm_cfg<NT, 2, 4>(gated);
+  if (wn == 4 && wk == 2) return ctas_per_sm_cfg<NT, 4, 2>(gated);
+  if (wn == 1 && wk == 4) return ctas_per_sm_cfg<NT, 1, 4>(gated);
+  return 2;
+}
+
+int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated) {
+  switch (nt) {
+    case 1: return ctas_per_sm_nt<1>(wn, wk, gated);
+    case 2: return ctas_per_sm_nt<2>(wn, wk, gated);
+    case 4: return ctas_per_sm_nt<4>(wn, wk, gated);
+    default: return 2;
+  }
+}
+
 cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s) {
   switch (p.nt) {
     case 1: return launch_nt<1>(a, p, workspace, s);

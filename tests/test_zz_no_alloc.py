@@ -74,7 +74,7 @@ def test_no_alloc_matches_workspace_entry_point():
     stream = torch.cuda.current_stream(dev).cuda_stream
     # split-K plans of several shapes (the scratch is really used) and one
     # without split-K
-    for i, (M, N, K) in enumerate([(8, 1024, 28672), (16, 4096, 4096), (1, 512, 8192), (4, 14336, 4096)]):
+    for i, (M, N, K) in enumerate([(8, 1024, 28672), (16, 1024, 4096), (1, 512, 8192), (4, 14336, 4096)]):
         x, q, s, b = _problem(M, N, K, 100 + i, dev)
         y_ws = _with_workspace(lib, x, q, s, b, stream)
         ref = x.float() @ (q.float() * s.float()[:, None]).t() + b.float()
@@ -90,7 +90,9 @@ def test_no_alloc_rejects_oversized_scratch():
     lib = _lib()
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    M, N, K = 32, 4096, 4096            # split-K plan needs 1 MiB + 4 KiB > the 1 MiB array
+    # a short-K layer: its split-K plan (3 slices of 32 x 4096 fp32 partial
+    # sums, 1.5 MiB + 4 KiB) is larger than the 1 MiB array
+    M, N, K = 32, 4096, 960
     x, q, s, b = _problem(M, N, K, 7, dev)
     y = torch.zeros(M, N, dtype=torch.float16, device=dev)
     torch.cuda.synchronize()
