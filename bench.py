@@ -240,7 +240,8 @@ def measure_mlp_block(ra, _capi, dev, capture, timed, peaks, args):
                 up = ra.int8_gemm(h, mlp.w_up.weight_int8, mlp.w_up.scale)
                 ra.int8_gemm(torch.nn.functional.silu(gate) * up, mlp.w_down.weight_int8, mlp.w_down.scale)
 
-        steps = 2000 if M == 8 else 100
+        # (scaled with --steps, so that a short run stays short under a profiler)
+        steps = max(20, min(2000, args.steps // 10)) if M == 8 else max(10, min(100, args.steps // 200))
         res = {}
         for name, fn in (("fused", fused), ("unfused", unfused)):
             gph = capture(fn)

@@ -106,20 +106,25 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
   const int sms = device_sm_count();
   if (aligned && K % 16 == 0 && M <= 32) {
     const int choice = g_decode_kernel.load(std::memory_order_relaxed);
+    Plan sk;
+    skinny_shape(sk, M, N, K, have_workspace, sms);
     // Measured on B200 (CUDA graphs of back-to-back launches): the persistent
-    // stream-K kernel wins on large weights, and from M = 9 on weights of
-    // 40 MB or more; the skinny kernel wins on smaller layers and on narrow
-    // column shards (lower fixed cost per launch).
+    // stream-K kernel wins on weights of 120 MB or more, and from M = 9 on
+    // weights of 40 MB or more when the skinny grid needs more than one wave
+    // of resident CTAs (e.g. M = 16: 4096 -> 11008 stream 18.9 us vs skinny
+    // 21.0 us; 11008 -> 4096, one skinny wave, skinny 18.4 us vs 20.5 us).
+    // The skinny kernel wins on smaller layers and on narrow column shards
+    // (lower fixed cost per launch).
     const double wbytes = static_cast<double>(N) * static_cast<double>(K);
-    const bool stream_wins = M <= 16 && ((M > 8 && wbytes >= 40e6) || wbytes >= 120e6);
+    const bool multi_wave = sk.grid_x > (int64_t)skinny_ctas_per_sm(sk.nt, sk.wn, sk.wk, false) * sms;
+    const bool stream_wins = M <= 16 && ((M > 8 && wbytes >= 40e6 && multi_wave) || wbytes >= 120e6);
     const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
     // The stream kernel keeps one arrival counter per CTA in the counter region.
     if (have_workspace && want_stream && sms <= kMaxSplitRowBlocks) {
       stream_shape(p, M, N, K, sms);
       return p;
     }
-    skinny_shape(p, M, N, K, have_workspace, sms);
-    return p;
+    return sk;
   }
   if (aligned && M > 32) {
     p.kernel = RLA_KERNEL_TCGEN05;
