@@ -59,24 +59,41 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   }
   const int rows = 16 * p.wn;
   p.grid_x = static_cast<int>((N + rows - 1) / rows);
+  // A grid of more 256-thread CTAs than fit on the GPU at once runs a second,
+  // mostly empty wave; 128-thread CTAs (four k-warps) fit about twice as many
+  // per SM.  Measured on B200 (M = 1): 4096 -> 11008, 688 CTAs, 15.7 -> 11.1 us;
+  // 4096 -> 14336, 896 CTAs, 16.4 -> 12.1 us.
+  if (p.wn == 1 && p.wk == 8 && p.grid_x > (int64_t)skinny_ctas_per_sm(p.nt, 1, 8, gated) * sms &&
+      p.grid_x <= (int64_t)skinny_ctas_per_sm(p.nt, 1, 4, gated) * sms)
+    p.wk = 4;
   p.splits = 1;
+  p.cluster = 0;
   // Split K only as far as the whole grid stays resident at once (one wave):
   // measured on B200, a second wave costs more than the extra parallelism
   // gains (e.g. 4096 x 4096 at M = 16: 7.7 us unsplit vs 10.9 us with two
   // slices at two resident CTAs per SM; at M = 1, four per SM, two slices win).
   const int64_t resident = (int64_t)skinny_ctas_per_sm(p.nt, p.wn, p.wk, gated) * sms;
-  if (have_ws && p.grid_x < resident && p.grid_x <= kMaxSplitRowBlocks) {
+  if (p.grid_x < resident) {
     // Each CTA slice should still give every k-warp a few chunks.
     const int64_t max_splits = chunks / (2 * p.wk);
     int64_t s = resident / p.grid_x;
     if (s > max_splits) s = max_splits;
     if (s > 32) s = 32;
-    if (s > 1) p.splits = static_cast<int>(s);
+    if (s > 1) {
+      if (s <= kMaxClusterSplits || !have_ws || p.grid_x > kMaxSplitRowBlocks) {
+        // the slices of a row block are one thread-block cluster and add up
+        // through distributed shared memory: no workspace, no global round trip
+        p.splits = static_cast<int>(s < kMaxClusterSplits ? s : kMaxClusterSplits);
+        p.cluster = 1;
+      } else {
+        p.splits = static_cast<int>(s);  // fp32 partial sums in the workspace
+      }
+    }
   }
   p.grid_y = p.splits;
   p.threads = 32 * p.wn * p.wk;
   p.smem = 0;
-  if (p.splits > 1) p.workspace = kSplitCounterBytes + (size_t)p.splits * (size_t)M * (size_t)N * 4;
+  if (p.splits > 1 && !p.cluster) p.workspace = kSplitCounterBytes + (size_t)p.splits * (size_t)M * (size_t)N * 4;
 }
 
 static std::atomic<int> g_decode_kernel{RLA_KERNEL_NONE};

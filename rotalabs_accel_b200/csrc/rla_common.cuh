@@ -129,6 +129,49 @@ RLA_DEVFN void rla_griddep_launch_dependents() { asm volatile("griddepcontrol.la
 // Pull the cache line holding `p` into L2 (never stale: L2 is coherent).
 RLA_DEVFN void rla_prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
+// Scalar loads issued where they stand (volatile: not sunk to their first
+// use), so that their latency overlaps the weight stream.
+RLA_DEVFN float rla_ldg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+RLA_DEVFN float rla_ldg_h2f(const __half* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.b16 %0, [%1];" : "=h"(v) : "l"(p));
+  return __half2float(__ushort_as_half(v));
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters: rank, barrier, distributed shared memory.
+// ---------------------------------------------------------------------------
+RLA_DEVFN uint32_t rla_cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+RLA_DEVFN uint32_t rla_cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster: stores before it are visible to
+// the cluster's loads after it.
+RLA_DEVFN void rla_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 16-byte load from CTA `rank`'s copy of the shared variable at `p`.
+RLA_DEVFN float4 rla_ld_dsmem_f4(const void* p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // Shared memory / mbarrier
 // ---------------------------------------------------------------------------

@@ -65,6 +65,7 @@ struct Plan {
   int wn = 0;      // 16-row groups of w per CTA
   int wk = 0;      // k-slicing warps per CTA
   int splits = 1;  // CTAs along K (split-K across CTAs when > 1)
+  int cluster = 0; // split-K inside a thread-block cluster of `splits` CTAs (no workspace)
   // tcgen05 kernel
   int bm = 0;      // rows of x per tile (MMA N)
   int stages = 0;  // TMA pipeline depth
@@ -79,6 +80,8 @@ struct Plan {
 // block, zero between calls; then the fp32 partial sums [splits][M][N].
 constexpr size_t kSplitCounterBytes = 4096;
 constexpr int kMaxSplitRowBlocks = static_cast<int>(kSplitCounterBytes / sizeof(unsigned int));
+// Largest split-K done inside one thread-block cluster (the portable cluster size).
+constexpr int kMaxClusterSplits = 8;
 
 Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace);
 

@@ -87,7 +87,9 @@ __global__ void __launch_bounds__(32 * WN * WK)
   for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
 
   // Let the next launch in the stream start, warm L2 with this lane's first
-  // batch of weight bytes, then wait for the predecessor before any real read.
+  // batch of weight bytes (and k-warp 0 with the scales and biases of its
+  // outputs, read by the epilogue), then wait for the predecessor before any
+  // real read.
   rla_griddep_launch_dependents();
 #pragma unroll
   for (int u = 0; u < U; ++u) {
@@ -97,10 +99,20 @@ __global__ void __launch_bounds__(32 * WN * WK)
       rla_prefetch_l2(wrow1 + cc * 64);
     }
   }
+  if (wk == 0 && q == 0) {
+    const int esz = scale_f32 ? 4 : 2, bsz = bias_kind == 2 ? 4 : 2;
+    rla_prefetch_l2(static_cast<const char*>(scale) + (int64_t)r0 * esz);
+    rla_prefetch_l2(static_cast<const char*>(GLU ? scale_up : scale) + (int64_t)r1 * esz);
+    if (bias_kind != 0) {
+      rla_prefetch_l2(static_cast<const char*>(bias) + (int64_t)r0 * bsz);
+      rla_prefetch_l2(static_cast<const char*>(GLU ? bias_up : bias) + (int64_t)r1 * bsz);
+    }
+  }
   rla_griddep_wait();
   unsigned int call = 0;
   if constexpr (PEER) call = peer_call(po);
   __shared__ int peer_slot;
+
 
   const uint4 zero4 = make_uint4(0, 0, 0, 0);
   for (int c = c_begin + wk; c < c_end; c += WK * U) {
@@ -141,7 +153,7 @@ __global__ void __launch_bounds__(32 * WN * WK)
   }
 
   // ---- reduce the WK k-slicing warps (fixed order) ----
-  __shared__ float red[(WK > 1 ? WK - 1 : 1) * WN * NT * 4 * 32];
+  __shared__ __align__(16) float red[(WK > 1 ? WK - 1 : 1) * WN * NT * 4 * 32];
   if constexpr (WK > 1) {
     if (wk > 0) {
       float* dst = red + (((wk - 1) * WN + wn) * NT * 4) * 32;
@@ -162,9 +174,46 @@ __global__ void __launch_bounds__(32 * WN * WK)
     }
   }
 
+  // ---- split-K inside a thread-block cluster (no workspace) ----
+  // The CTAs of a row block form one cluster along y, cluster rank = K slice.
+  // Ranks 1.. leave k-warp 0's partial sums in shared memory; rank 0 adds
+  // them in rank order (the order of the workspace path below, so the sums
+  // are the same) and runs the single-CTA epilogue.
+  const bool cluster_split = gridDim.y > 1 && partial == nullptr;
+  if (cluster_split) {
+    static_assert(WK >= 2, "the exchange reuses the k-warp reduction buffer");
+    float* mine = red + (wn * 32 + lane) * (NT * 4);  // (WN x 32 lanes) x (NT x 4) floats
+    const uint32_t rank = rla_cluster_ctarank();
+    __syncwarp();  // this warp's reads of the reduction buffer are done
+    if (wk == 0 && rank != 0) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        *reinterpret_cast<float4*>(mine + 4 * t) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+    }
+    rla_cluster_sync();
+    if (wk == 0 && rank == 0) {
+      const uint32_t ranks = rla_cluster_nctarank();
+      for (uint32_t r = 1; r < ranks; ++r) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const float4 v = rla_ld_dsmem_f4(mine + 4 * t, r);
+          acc[t][0] += v.x;
+          acc[t][1] += v.y;
+          acc[t][2] += v.z;
+          acc[t][3] += v.w;
+        }
+      }
+    }
+    rla_cluster_sync();  // no CTA exits while rank 0 may still read its shared memory
+    if (rank != 0) {
+      if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
+      return;
+    }
+  }
+
   // Accumulator element (t, i): row n = n0 + g + 8*(i>>1), token m = 8t + 2q + (i&1).
   // Gated form: i>>1 = 0 is the gate, 1 the up projection of output n0 + g.
-  if (gridDim.y == 1) {
+  if (gridDim.y == 1 || cluster_split) {
     if constexpr (GLU) {
       const int n = n0 + g;
       if (wk == 0 && n < N) {
@@ -310,7 +359,7 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
   const int cps = (total_chunks + p.splits - 1) / p.splits;
   unsigned int* counters = nullptr;
   float* partial = nullptr;
-  if (p.splits > 1) {
+  if (p.splits > 1 && !p.cluster) {
     counters = static_cast<unsigned int*>(workspace);
     partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kSplitCounterBytes);
   }
@@ -319,11 +368,20 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
   cfg.blockDim = dim3(32 * WN * WK);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see rla_griddep_wait
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (p.splits > 1 && p.cluster) {
+    // the K slices of a row block are one cluster (split-K through
+    // distributed shared memory)
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = static_cast<unsigned int>(p.splits);
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   auto kern = a.w_up ? w8a16_skinny_kernel<NT, WN, WK, U, false, true>
               : a.peer.world > 0 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false>
                                  : w8a16_skinny_kernel<NT, WN, WK, U, false, false>;

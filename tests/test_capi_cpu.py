@@ -90,10 +90,16 @@ def test_selector_rules(lib):
             assert p["x_rows"] >= M and p["x_rows"] <= 32
             if p["kernel_name"] == "skinny":
                 assert p["grid_x"] * p["w_rows"] >= N
-    # narrow column shards with long K get split-K across CTAs
+    # narrow column shards with long K get split-K across CTAs; without a
+    # workspace the slices add up inside a thread-block cluster (at most 8)
     p = _capi.plan(1, 1024, 28672)
     assert p["kernel_name"] == "skinny" and p["splits"] > 1
-    assert _capi.plan(1, 1024, 28672, have_workspace=False)["splits"] == 1
+    p = _capi.plan(1, 1024, 28672, have_workspace=False)
+    assert p["kernel_name"] == "skinny" and 1 < p["splits"] <= 8
+    # split-K plans of up to 8 slices need no workspace (cluster exchange)
+    lib = _capi.load_library()
+    assert _capi.plan(1, 4096, 4096)["splits"] <= 8
+    assert lib.rla_w8a16_workspace_size(32, 4096, 960) == 0
     # prefill regime -> tcgen05
     for K, N in ((4096, 12288), (4096, 11008), (11008, 4096)):
         p = _capi.plan(2048, N, K)
@@ -124,10 +130,15 @@ def test_selector_rules(lib):
 
 def test_workspace_size(lib):
     assert lib.rla_w8a16_workspace_size(2048, 4096, 4096) == 0
-    p = _capi.plan(1, 1024, 28672)
-    need = lib.rla_w8a16_workspace_size(1, 1024, 28672)
-    assert need >= p["splits"] * 1 * 1024 * 4
+    # more than 8 slices: fp32 partial sums in the workspace
+    p = _capi.plan(1, 256, 28672)
+    assert p["splits"] > 8
+    need = lib.rla_w8a16_workspace_size(1, 256, 28672)
+    assert need >= p["splits"] * 1 * 256 * 4
     assert need % 4 == 0
+    # up to 8 slices: a thread-block cluster, no workspace
+    assert 1 < _capi.plan(1, 1024, 28672)["splits"] <= 8
+    assert lib.rla_w8a16_workspace_size(1, 1024, 28672) == 0
 
 
 def test_cuda_path_never_falls_back(monkeypatch):

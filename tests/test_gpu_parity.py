@@ -248,13 +248,36 @@ def test_deterministic_split_k(dev):
     _check(y1, _fp32_ref(x, q, s))
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (8, 512, 8192), (16, 1024, 4096), (32, 4096, 960),
+                                   (3, 1000, 4096), (1, 128, 28672), (8, 256, 28672)])
+@pytest.mark.parametrize("bias", [None, "f32"])
+def test_split_k_cluster_and_workspace_paths(dev, M, N, K, bias):
+    """Split-K of up to 8 slices adds the slices inside a thread-block
+    cluster (no workspace); more slices add fp32 partial sums in the
+    workspace.  Both are bit-identical from run to run and within the bar."""
+    from rotalabs_accel_b200 import int8_gemm, _capi
+    x, q, s = _problem(M, N, K, seed=M + N + K, scale_dtype=torch.float32)
+    b = (torch.randn(N, device=dev) * 0.1) if bias == "f32" else None
+    p = _capi.plan(M, N, K)
+    ws = _capi.load_library().rla_w8a16_workspace_size(M, N, K)
+    if p["kernel_name"] == "skinny" and p["splits"] > 1:
+        assert (ws == 0) == (p["splits"] <= 8), (p, ws)
+    y1 = int8_gemm(x, q, s, b)
+    y2 = int8_gemm(x, q, s, b)
+    assert torch.equal(y1, y2)
+    _check(y1, _fp32_ref(x, q, s, b))
+    assert _capi.device_error() == 0
+
+
 def test_workspace_shared_across_shapes(dev):
     """Split-K calls of different shapes share one workspace: the fixed
     counter region must not overlap an earlier call's partial sums."""
     from rotalabs_accel_b200 import int8_gemm, _capi
     # (narrow layers: the selector splits K only while the grid stays one wave)
+    # (up to 8 slices add up in a thread-block cluster and leave the workspace
+    # alone; (1, 128, 28672) and (8, 256, 28672) split further, through it)
     shapes = [(4, 256, 1024), (16, 1024, 4096), (1, 1024, 28672), (16, 256, 4096), (8, 512, 8192),
-              (1, 2048, 4096), (32, 512, 4096)]
+              (1, 2048, 4096), (32, 512, 4096), (1, 128, 28672), (8, 256, 28672)]
     probs = [_problem(M, N, K, seed=i) for i, (M, N, K) in enumerate(shapes)]
     # the two decode kernels use the same workspace with the same fixed layout
     for kern in ("skinny", "stream", "skinny", "stream"):

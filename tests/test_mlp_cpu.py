@@ -129,7 +129,8 @@ def test_capi_rejects_bad_arguments(lib):
 def test_gated_workspace_sizes(lib):
     # decode: the skinny plan for 2N rows (split-K partials of gate and up)
     assert lib.rla_w8a16_swiglu_workspace_size(8, 11008, 4096) % 4 == 0
-    assert lib.rla_w8a16_swiglu_workspace_size(8, 256, 4096) > 4096           # narrow: split-K
+    assert lib.rla_w8a16_swiglu_workspace_size(8, 256, 4096) == 0             # narrow: split-K in a cluster
+    assert lib.rla_w8a16_swiglu_workspace_size(8, 128, 28672) > 4096          # > 8 slices: workspace partials
     # prefill: the counter region, then fp16 gate and up outputs, each padded to 256 bytes
     assert lib.rla_w8a16_swiglu_workspace_size(2048, 11008, 4096) == 4096 + 2 * 2048 * 11008 * 2
     assert lib.rla_w8a16_swiglu_workspace_size(33, 3, 64) == 4096 + 2 * 256
