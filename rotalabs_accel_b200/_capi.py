@@ -5,6 +5,11 @@ The shared library ``librla_w8a16.so`` is built in-tree
 Every CUDA computation of the package goes through here; if the library is
 missing or does not load, calls raise instead of computing anything another
 way.
+
+The per-token hot calls (``w8a16_gemm``, ``w8a16_gemm_swiglu``) go through
+``_rla_fast``, CPython fast-call bindings of the same entry points linked to
+the same library (ctypes' generic argument conversion costs more host time
+than a decode GEMM takes on the GPU).  Without that module they use ctypes.
 """
 
 from __future__ import annotations
@@ -36,6 +41,7 @@ PEER_SYNC_BYTES = 512
 IPC_HANDLE_BYTES = 64
 
 _lib = None
+_fast = None
 _lib_lock = threading.Lock()
 
 
@@ -101,6 +107,14 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.rla_w8a16_swiglu_workspace_size.restype = sz
         lib.rla_rmsnorm.argtypes = [p, i64, p, ctypes.c_int, ctypes.c_float, p, i64, i64, i64, p]
         lib.rla_rmsnorm.restype = ctypes.c_int
+        if os.path.abspath(path) == LIB_PATH:
+            # linked to this library by soname: the loader reuses the copy
+            # loaded above, so both bindings share one library state
+            try:
+                from . import _rla_fast
+                globals()["_fast"] = _rla_fast
+            except ImportError:
+                pass
         _lib = lib
         return lib
 
@@ -162,24 +176,32 @@ def w8a16_gemm(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor
     ``x2d`` fp16 ``[M, K]`` with unit inner stride; ``weight_int8`` int8
     ``[N, K]`` with unit inner stride; ``scale`` ``[N]`` fp32/fp16
     contiguous; ``bias`` ``[N]`` fp16/fp32 or None."""
-    lib = load_library()
+    lib = _lib if _lib is not None else load_library()
+    fast = _fast
     M, K = x2d.shape
     N = weight_int8.shape[0]
+    device = x2d.device
     if out is None:
-        out = torch.empty((M, N), dtype=torch.float16, device=x2d.device)
-    stream = torch.cuda.current_stream(x2d.device).cuda_stream
-    need = lib.rla_w8a16_workspace_size(M, N, K)
-    ws_ptr, ws_bytes = None, 0
+        out = torch.empty((M, N), dtype=torch.float16, device=device)
+    index = device.index
+    stream = torch._C._cuda_getCurrentRawStream(index)
+    need = fast.workspace_size(M, N, K) if fast is not None else lib.rla_w8a16_workspace_size(M, N, K)
+    ws_ptr, ws_bytes = 0, 0
     if need:
-        ws = _workspace(x2d.device, stream, need)
+        ws = _workspace(device, stream, need)
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
-    with torch.cuda.device(x2d.device):
-        st = lib.rla_w8a16_gemm(
-            x2d.data_ptr(), x2d.stride(0) if M > 0 else K, weight_int8.data_ptr(),
+    args = (x2d.data_ptr(), x2d.stride(0) if M > 0 else K, weight_int8.data_ptr(),
             weight_int8.stride(0) if N > 0 else K, scale.data_ptr(), _scale_dtype(scale),
-            bias.data_ptr() if bias is not None else None, _bias_dtype(bias),
+            bias.data_ptr() if bias is not None else 0, _bias_dtype(bias),
             out.data_ptr(), out.stride(0) if M > 0 else N, M, N, K, ws_ptr, ws_bytes, stream)
-    _check(st, "rla_w8a16_gemm")
+    call = fast.gemm if fast is not None else lib.rla_w8a16_gemm
+    if index == torch.cuda.current_device():
+        st = call(*args)
+    else:
+        with torch.cuda.device(device):
+            st = call(*args)
+    if st != RLA_OK:
+        _check(st, "rla_w8a16_gemm")
     return out
 
 
@@ -201,19 +223,24 @@ def w8a16_gemm_swiglu(x2d: torch.Tensor, w_gate: torch.Tensor, scale_gate: torch
         raise TypeError("bias_gate and bias_up must both be given (same dtype) or both be None")
     if out is None:
         out = torch.empty((M, N), dtype=torch.float16, device=x2d.device)
-    stream = torch.cuda.current_stream(x2d.device).cuda_stream
+    index = x2d.device.index
+    stream = torch._C._cuda_getCurrentRawStream(index)
     need = lib.rla_w8a16_swiglu_workspace_size(M, N, K)
-    ws_ptr, ws_bytes = None, 0
+    ws_ptr, ws_bytes = 0, 0
     if need:
         ws = _workspace(x2d.device, stream, need)
         ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
-    with torch.cuda.device(x2d.device):
-        st = lib.rla_w8a16_gemm_swiglu(
-            x2d.data_ptr(), x2d.stride(0) if M > 0 else K, w_gate.data_ptr(), w_up.data_ptr(),
+    args = (x2d.data_ptr(), x2d.stride(0) if M > 0 else K, w_gate.data_ptr(), w_up.data_ptr(),
             w_gate.stride(0) if N > 0 else K, scale_gate.data_ptr(), scale_up.data_ptr(), _scale_dtype(scale_gate),
-            bias_gate.data_ptr() if bias_gate is not None else None,
-            bias_up.data_ptr() if bias_up is not None else None, _bias_dtype(bias_gate),
+            bias_gate.data_ptr() if bias_gate is not None else 0,
+            bias_up.data_ptr() if bias_up is not None else 0, _bias_dtype(bias_gate),
             out.data_ptr(), out.stride(0) if M > 0 else N, M, N, K, ws_ptr, ws_bytes, stream)
+    call = _fast.gemm_swiglu if _fast is not None else lib.rla_w8a16_gemm_swiglu
+    if index == torch.cuda.current_device():
+        st = call(*args)
+    else:
+        with torch.cuda.device(x2d.device):
+            st = call(*args)
     _check(st, "rla_w8a16_gemm_swiglu")
     return out
 

@@ -7,6 +7,10 @@ the C ABI of ``include/rla_w8a16.h``) with nvcc for ``sm_100a`` into
 ``rotalabs_accel_b200/librla_w8a16.so``.  The CUDA runtime is linked
 statically; the driver's tensor-map encoder is reached through
 ``cudaGetDriverEntryPoint`` so nothing links ``libcuda`` directly.
+
+Then compiles ``csrc/rla_pyfast.c``, the CPython fast-call bindings of the
+hot entry points, with the host C compiler into ``_rla_fast<EXT_SUFFIX>``
+next to the library, linked to it by soname with an ``$ORIGIN`` rpath.
 """
 
 from __future__ import annotations
@@ -15,11 +19,13 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "librla_w8a16.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
+FAST_PATH = os.path.join(HERE, "_rla_fast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -27,6 +33,7 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     "-shared", "-cudart", "static",
     "--expt-relaxed-constexpr",
+    "-Xlinker", "-soname=" + LIB_NAME,
 ]
 
 
@@ -37,6 +44,13 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found: the sm_100a library cannot be built")
 
 
+def _cc() -> str:
+    for cand in (os.environ.get("CC"), shutil.which("gcc"), shutil.which("cc")):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("no host C compiler found for the fast-call bindings")
+
+
 def _sources():
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC)
                   if f.endswith((".cu", ".cuh", ".h"))) + \
@@ -44,10 +58,24 @@ def _sources():
 
 
 def needs_build() -> bool:
-    if not os.path.exists(LIB_PATH):
+    if not os.path.exists(LIB_PATH) or not os.path.exists(FAST_PATH):
         return True
-    t = os.path.getmtime(LIB_PATH)
-    return any(os.path.getmtime(s) > t for s in _sources())
+    t = min(os.path.getmtime(LIB_PATH), os.path.getmtime(FAST_PATH))
+    return any(os.path.getmtime(s) > t for s in _sources() + [os.path.join(CSRC, "rla_pyfast.c")])
+
+
+def build_fast(verbose: bool = False) -> str:
+    """Compile the CPython fast-call module against the built library."""
+    tmp = FAST_PATH + ".tmp"
+    cmd = [_cc(), "-O2", "-shared", "-fPIC", "-std=c11", "-I" + sysconfig.get_paths()["include"],
+           os.path.join(CSRC, "rla_pyfast.c"), "-L" + HERE, "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN", "-o", tmp]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"building the fast-call bindings failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, FAST_PATH)
+    return FAST_PATH
 
 
 def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
@@ -64,6 +92,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
     if verbose and (r.stdout or r.stderr):
         print(r.stdout, r.stderr, file=sys.stderr)
     os.replace(tmp, LIB_PATH)
+    build_fast(verbose)
     return LIB_PATH
 
 

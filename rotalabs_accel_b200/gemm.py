@@ -78,8 +78,9 @@ def int8_gemm(x: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
     assert scale.shape == (N,), f"Scale shape mismatch: {scale.shape} vs ({N},)"
 
     if x.is_cuda and weight_int8.is_cuda and scale.is_cuda:
-        lead = x.shape[:-1]
-        x2 = _as_2d_fp16(x, K)
+        # (a 2-D fp16 x with unit inner stride, the per-token case, is used as is)
+        plain = x.dim() == 2 and x.dtype == torch.float16 and (x.shape[0] == 0 or x.stride(1) == 1)
+        x2 = x if plain else _as_2d_fp16(x, K)
         w = weight_int8 if (N == 0 or weight_int8.stride(1) == 1) else weight_int8.contiguous()
         s = scale if scale.is_contiguous() else scale.contiguous()
         b = None
@@ -87,7 +88,7 @@ def int8_gemm(x: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
             b = bias if bias.dtype in (torch.float16, torch.float32) else bias.to(torch.float16)
             b = b.contiguous()
         y = _capi.w8a16_gemm(x2, w, s, b)
-        return y.view(*lead, N)
+        return y if plain else y.view(*x.shape[:-1], N)
 
     return int8_gemm_torch(x, weight_int8, scale, bias)
 

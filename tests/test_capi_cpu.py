@@ -147,3 +147,26 @@ def test_cuda_path_never_falls_back(monkeypatch):
     monkeypatch.setattr(_capi, "_lib", None)
     with pytest.raises(RuntimeError, match="missing"):
         _capi.load_library("/nonexistent/librla_w8a16.so")
+
+
+def test_fast_call_bindings_share_the_library():
+    """The CPython fast-call module is linked to the same library instance as
+    the ctypes bindings: a status and error message set through one are seen
+    through the other, and the process maps one copy of the library."""
+    lib = _capi.load_library()
+    fast = _capi._fast
+    assert fast is not None, "rotalabs_accel_b200/_rla_fast is not built"
+    assert fast.workspace_size(1, 256, 28672) == lib.rla_w8a16_workspace_size(1, 256, 28672)
+    assert fast.workspace_size(2048, 4096, 4096) == 0
+    n0 = lib.rla_launch_count()
+    # M < 0: invalid argument, reported through the shared error string
+    assert fast.gemm(0, 0, 0, 0, 0, 1, 0, 0, 0, 0, -1, 64, 64, 0, 0, 0) == 1
+    assert b"M, N, K" in lib.rla_last_error()
+    assert fast.gemm_swiglu(0, 0, 0, 0, 0, 0, 0, 7, 0, 0, 0, 0, 0, 4, 64, 64, 0, 0, 0) == 1
+    assert b"scale_dtype" in lib.rla_last_error()
+    assert lib.rla_launch_count() == n0
+    with pytest.raises(TypeError):
+        fast.gemm(1, 2, 3)
+    maps = open("/proc/self/maps").read()
+    paths = {line.split()[-1] for line in maps.splitlines() if line.endswith("librla_w8a16.so")}
+    assert len(paths) == 1, paths
