@@ -87,8 +87,10 @@ RLA_API int rla_set_decode_kernel(int kernel);
  *          counters that must be zero before the first call (the library
  *          leaves them at zero after every call, so one workspace serves
  *          calls of any shape); fp32 partial sums follow.  May be NULL / 0:
- *          the selector then plans without split-K.  Calls that share a
- *          workspace must be stream-ordered.
+ *          the selector then plans split-K only inside thread-block
+ *          clusters (up to 8 slices, added through distributed shared
+ *          memory, which needs no workspace).  Calls that share a workspace
+ *          must be stream-ordered.
  *   stream cudaStream_t to launch on.
  *
  * Returns RLA_OK, or an error with nothing launched.
@@ -97,7 +99,8 @@ RLA_API int rla_w8a16_gemm(const void* x, int64_t ldx, const int8_t* w, int64_t 
                    int scale_dtype, const void* bias, int bias_dtype, void* y, int64_t ldy, int64_t M,
                    int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Bytes of workspace the selector's plan for (M, N, K) can use (0 if none).
+/* Bytes of workspace the selector's plan for (M, N, K) can use (0 if none:
+ * no split-K, or split-K inside thread-block clusters).
  * Part of the same replacement as rla_w8a16_gemm (gemm.py:140-186). */
 RLA_API size_t rla_w8a16_workspace_size(int64_t M, int64_t N, int64_t K);
 
