@@ -59,12 +59,13 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   }
   const int rows = 16 * p.wn;
   p.grid_x = static_cast<int>((N + rows - 1) / rows);
-  // A grid of more 256-thread CTAs than fit on the GPU at once runs a second,
+  // A grid of more 256-thread CTAs than fit on the GPU at once runs a last,
   // mostly empty wave; 128-thread CTAs (four k-warps) fit about twice as many
-  // per SM.  Measured on B200 (M = 1): 4096 -> 11008, 688 CTAs, 15.7 -> 11.1 us;
-  // 4096 -> 14336, 896 CTAs, 16.4 -> 12.1 us.
-  if (p.wn == 1 && p.wk == 8 && p.grid_x > (int64_t)skinny_ctas_per_sm(p.nt, 1, 8, gated) * sms &&
-      p.grid_x <= (int64_t)skinny_ctas_per_sm(p.nt, 1, 4, gated) * sms)
+  // per SM and shorten or remove it.  Measured on B200: 4096 -> 11008 at
+  // M = 1, 688 CTAs, 15.7 -> 11.1 us; 4096 -> 14336 at M = 1, 896 CTAs,
+  // 16.4 -> 12.1 us; the gated 4096 -> 2 x 11008 at M = 16, 1376 CTAs (more
+  // than one wave either way), 34.8 -> 28.3 us.
+  if (p.wn == 1 && p.wk == 8 && p.grid_x > (int64_t)skinny_ctas_per_sm(p.nt, 1, 8, gated) * sms)
     p.wk = 4;
   p.splits = 1;
   p.cluster = 0;
