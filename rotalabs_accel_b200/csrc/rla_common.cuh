@@ -129,19 +129,6 @@ RLA_DEVFN void rla_griddep_launch_dependents() { asm volatile("griddepcontrol.la
 // Pull the cache line holding `p` into L2 (never stale: L2 is coherent).
 RLA_DEVFN void rla_prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
-// Scalar loads issued where they stand (volatile: not sunk to their first
-// use), so that their latency overlaps the weight stream.
-RLA_DEVFN float rla_ldg_f32(const float* p) {
-  float v;
-  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
-  return v;
-}
-RLA_DEVFN float rla_ldg_h2f(const __half* p) {
-  unsigned short v;
-  asm volatile("ld.global.nc.b16 %0, [%1];" : "=h"(v) : "l"(p));
-  return __half2float(__ushort_as_half(v));
-}
-
 // ---------------------------------------------------------------------------
 // Thread-block clusters: rank, barrier, distributed shared memory.
 // ---------------------------------------------------------------------------
