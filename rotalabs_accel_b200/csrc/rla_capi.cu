@@ -67,13 +67,22 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   // than one wave either way), 34.8 -> 28.3 us.
   if (p.wn == 1 && p.wk == 8 && p.grid_x > (int64_t)skinny_ctas_per_sm(p.nt, 1, 8, gated) * sms)
     p.wk = 4;
+  // M = 9..16 in 128-thread CTAs: loading each chunk's activations just
+  // before its MMAs costs registers (fewer CTAs fit per SM) but streams
+  // faster; used while the grid still fits in one wave.  Measured on B200,
+  // 4096 -> 11008 at M = 16: 18.1 -> 15.2 us; 4096 -> 14336 (896 CTAs, one
+  // more than fit) would need a second wave: 26.2 us against 18.6 without.
+  p.xjit = 0;
+  if (p.nt == 2 && p.wn == 1 && p.wk == 4 && !gated &&
+      p.grid_x <= (int64_t)skinny_ctas_per_sm(p.nt, 1, 4, false, true) * sms)
+    p.xjit = 1;
   p.splits = 1;
   p.cluster = 0;
   // Split K only as far as the whole grid stays resident at once (one wave):
   // measured on B200, a second wave costs more than the extra parallelism
   // gains (e.g. 4096 x 4096 at M = 16: 7.7 us unsplit vs 10.9 us with two
   // slices at two resident CTAs per SM; at M = 1, four per SM, two slices win).
-  const int64_t resident = (int64_t)skinny_ctas_per_sm(p.nt, p.wn, p.wk, gated) * sms;
+  const int64_t resident = (int64_t)skinny_ctas_per_sm(p.nt, p.wn, p.wk, gated, p.xjit != 0) * sms;
   if (p.grid_x < resident) {
     // Each CTA slice should still give every k-warp a few chunks.
     const int64_t max_splits = chunks / (2 * p.wk);
@@ -134,7 +143,7 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
     // The skinny kernel wins on smaller layers and on narrow column shards
     // (lower fixed cost per launch).
     const double wbytes = static_cast<double>(N) * static_cast<double>(K);
-    const bool multi_wave = sk.grid_x > (int64_t)skinny_ctas_per_sm(sk.nt, sk.wn, sk.wk, false) * sms;
+    const bool multi_wave = sk.grid_x > (int64_t)skinny_ctas_per_sm(sk.nt, sk.wn, sk.wk, false, sk.xjit != 0) * sms;
     const bool stream_wins = M <= 16 && ((M > 8 && wbytes >= 40e6 && multi_wave) || wbytes >= 120e6);
     const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
     // The stream kernel keeps one arrival counter per CTA in the counter region.

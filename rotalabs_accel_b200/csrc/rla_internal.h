@@ -66,6 +66,7 @@ struct Plan {
   int wk = 0;      // k-slicing warps per CTA
   int splits = 1;  // CTAs along K (split-K across CTAs when > 1)
   int cluster = 0; // split-K inside a thread-block cluster of `splits` CTAs (no workspace)
+  int xjit = 0;    // NT = 2, (1, 4): activation loads just before the MMAs
   // tcgen05 kernel
   int bm = 0;      // rows of x per tile (MMA N)
   int stages = 0;  // TMA pipeline depth
@@ -92,7 +93,7 @@ void set_error(const char* fmt, ...);
 cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
 // Resident CTAs per SM of the skinny kernel instance (plain or gated form);
 // 2 when the device cannot be queried.
-int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated);
+int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit = false);
 cudaError_t launch_stream(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
 size_t stream_workspace_bytes(int64_t M, int ctas);
 size_t stream_smem_bytes(int nt);

@@ -45,7 +45,7 @@ struct XFrag {
   uint4 v[NT][2];
 };
 
-template <int NT, int WN, int WK, int U, bool PEER, bool GLU>
+template <int NT, int WN, int WK, int U, bool PEER, bool GLU, bool XJ>
 __global__ void __launch_bounds__(32 * WN * WK)
     w8a16_skinny_kernel(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,
                         const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias,
@@ -115,6 +115,11 @@ __global__ void __launch_bounds__(32 * WN * WK)
 
 
   const uint4 zero4 = make_uint4(0, 0, 0, 0);
+  // XJIT: each chunk's activation fragments are loaded just before its MMAs
+  // instead of with the batch's weight loads, so that all the weight loads
+  // issue first.  Chosen per launch shape (XJ) from measurements; the gated
+  // and exchange forms keep the batch order.
+  constexpr bool XJIT = XJ && !PEER && !GLU;
   for (int c = c_begin + wk; c < c_end; c += WK * U) {
     uint4 wa[U][2];
     XFrag<NT> xb[U];
@@ -127,15 +132,28 @@ __global__ void __launch_bounds__(32 * WN * WK)
       const bool ok = (cc < c_end) && (kofs + q * 16 < K);
       wa[u][0] = ok ? rla_ldg_stream(wrow0 + kofs) : zero4;
       wa[u][1] = ok ? rla_ldg_stream(wrow1 + kofs) : zero4;
+      if constexpr (!XJIT) {
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        const bool okx = ok && xrow_ok[t];
-        xb[u].v[t][0] = okx ? rla_ldg_keep(xrow[t] + kofs) : zero4;
-        xb[u].v[t][1] = okx ? rla_ldg_keep(xrow[t] + kofs + 8) : zero4;
+        for (int t = 0; t < NT; ++t) {
+          const bool okx = ok && xrow_ok[t];
+          xb[u].v[t][0] = okx ? rla_ldg_keep(xrow[t] + kofs) : zero4;
+          xb[u].v[t][1] = okx ? rla_ldg_keep(xrow[t] + kofs + 8) : zero4;
+        }
       }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
+      if constexpr (XJIT) {
+        const int cc = c + u * WK;
+        const int kofs = cc * 64;
+        const bool ok = (cc < c_end) && (kofs + q * 16 < K);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const bool okx = ok && xrow_ok[t];
+          xb[u].v[t][0] = okx ? rla_ldg_keep(xrow[t] + kofs) : zero4;
+          xb[u].v[t][1] = okx ? rla_ldg_keep(xrow[t] + kofs + 8) : zero4;
+        }
+      }
       const uint32_t* w0 = reinterpret_cast<const uint32_t*>(&wa[u][0]);
       const uint32_t* w1 = reinterpret_cast<const uint32_t*>(&wa[u][1]);
 #pragma unroll
@@ -353,7 +371,7 @@ __global__ void __launch_bounds__(32 * WN * WK)
   if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
 }
 
-template <int NT, int WN, int WK, int U>
+template <int NT, int WN, int WK, int U, bool XJ>
 static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s) {
   const int total_chunks = (a.K + 63) / 64;
   const int cps = (total_chunks + p.splits - 1) / p.splits;
@@ -382,9 +400,9 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
   }
-  auto kern = a.w_up ? w8a16_skinny_kernel<NT, WN, WK, U, false, true>
-              : a.peer.world > 0 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false>
-                                 : w8a16_skinny_kernel<NT, WN, WK, U, false, false>;
+  auto kern = a.w_up ? w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>
+              : a.peer.world > 0 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>
+                                 : w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>;
   PeerOut po = a.peer;
   if (po.world > 0) {
     // Unpacking CTAs: the whole grid when it is resident at once, else at
@@ -404,18 +422,25 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
                             a.N, a.K, cps, partial, counters, po, a.w_up, a.scale_up, a.bias_up);
 }
 
-// Instantiated configurations: NT in {1, 2, 4}; (WN, WK) in {(1, 8), (2, 4), (4, 2)}.
+// Instantiated configurations: NT in {1, 2, 4}; (WN, WK) in {(1, 8), (2, 4),
+// (4, 2), (1, 4)}.  Activation loads just before the MMAs (XJ): always for
+// NT = 1 with (1, 8); for NT = 2 with (1, 4) when the plan asks for it.
 template <int NT>
 static cudaError_t launch_nt(const GemmArgs& a, const Plan& p, void* ws, cudaStream_t s) {
   constexpr int U = NT >= 4 ? 2 : 4;
-  if (p.wn == 1 && p.wk == 8) return launch_cfg<NT, 1, 8, U>(a, p, ws, s);
-  if (p.wn == 2 && p.wk == 4) return launch_cfg<NT, 2, 4, U>(a, p, ws, s);
-  if (p.wn == 4 && p.wk == 2) return launch_cfg<NT, 4, 2, U>(a, p, ws, s);
-  if (p.wn == 1 && p.wk == 4) return launch_cfg<NT, 1, 4, U>(a, p, ws, s);
+  if (p.wn == 1 && p.wk == 8) return launch_cfg<NT, 1, 8, U, NT == 1>(a, p, ws, s);
+  if (p.wn == 2 && p.wk == 4) return launch_cfg<NT, 2, 4, U, false>(a, p, ws, s);
+  if (p.wn == 4 && p.wk == 2) return launch_cfg<NT, 4, 2, U, false>(a, p, ws, s);
+  if (p.wn == 1 && p.wk == 4) {
+    if constexpr (NT == 2) {
+      if (p.xjit) return launch_cfg<NT, 1, 4, U, true>(a, p, ws, s);
+    }
+    return launch_cfg<NT, 1, 4, U, false>(a, p, ws, s);
+  }
   return cudaErrorInvalidConfiguration;
 }
 
-template <int NT, int WN, int WK>
+template <int NT, int WN, int WK, bool XJ>
 static int ctas_per_sm_cfg(bool gated) {
   constexpr int U = NT >= 4 ? 2 : 4;
   static int cache[2] = {-1, -1};
@@ -423,10 +448,10 @@ static int ctas_per_sm_cfg(bool gated) {
   if (c < 0) {
     int v = 0;
     const cudaError_t e =
-        gated ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, w8a16_skinny_kernel<NT, WN, WK, U, false, true>,
-                                                              32 * WN * WK, 0)
-              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, w8a16_skinny_kernel<NT, WN, WK, U, false, false>,
-                                                              32 * WN * WK, 0);
+        gated ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                    &v, w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>, 32 * WN * WK, 0)
+              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                    &v, w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>, 32 * WN * WK, 0);
     if (e != cudaSuccess || v < 1) {
       (void)cudaGetLastError();
       return 2;   // no device to ask (e.g. planning on a CPU-only host)
@@ -437,19 +462,24 @@ static int ctas_per_sm_cfg(bool gated) {
 }
 
 template <int NT>
-static int ctas_per_sm_nt(int wn, int wk, bool gated) {
-  if (wn == 1 && wk == 8) return ctas_per_sm_cfg<NT, 1, 8>(gated);
-  if (wn == 2 && wk == 4) return ctas_per_sm_cfg<NT, 2, 4>(gated);
-  if (wn == 4 && wk == 2) return ctas_per_sm_cfg<NT, 4, 2>(gated);
-  if (wn == 1 && wk == 4) return ctas_per_sm_cfg<NT, 1, 4>(gated);
+static int ctas_per_sm_nt(int wn, int wk, bool gated, bool xjit) {
+  if (wn == 1 && wk == 8) return ctas_per_sm_cfg<NT, 1, 8, NT == 1>(gated);
+  if (wn == 2 && wk == 4) return ctas_per_sm_cfg<NT, 2, 4, false>(gated);
+  if (wn == 4 && wk == 2) return ctas_per_sm_cfg<NT, 4, 2, false>(gated);
+  if (wn == 1 && wk == 4) {
+    if constexpr (NT == 2) {
+      if (xjit) return ctas_per_sm_cfg<NT, 1, 4, true>(gated);
+    }
+    return ctas_per_sm_cfg<NT, 1, 4, false>(gated);
+  }
   return 2;
 }
 
-int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated) {
+int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit) {
   switch (nt) {
-    case 1: return ctas_per_sm_nt<1>(wn, wk, gated);
-    case 2: return ctas_per_sm_nt<2>(wn, wk, gated);
-    case 4: return ctas_per_sm_nt<4>(wn, wk, gated);
+    case 1: return ctas_per_sm_nt<1>(wn, wk, gated, xjit);
+    case 2: return ctas_per_sm_nt<2>(wn, wk, gated, xjit);
+    case 4: return ctas_per_sm_nt<4>(wn, wk, gated, xjit);
     default: return 2;
   }
 }
