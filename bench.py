@@ -5,21 +5,29 @@ M in {1, 4, 8, 16} x (K, N) in {(4096, 4096), (4096, 11008), (11008, 4096),
 (4096, 14336)}: 16 W8A16 GEMMs, each with its own int8 weight (663 MB of
 weights in all, > the 126 MB L2, so every GEMM streams its weight from HBM).
 x ~ N(0, 1) fp16, W ~ N(0, 0.02) quantized per output channel, fp16 scales,
-seeded synthetic data.  With N GPUs every layer is column-parallel: each
-rank holds N_layer / world output channels and runs its slice; by default
-(``--exchange p2p``) the decode kernel sends its slice to every peer over
-NVLink as flagged words and unpacks theirs in the same launch
-(``rla_w8a16_gemm_allgather``); ``--exchange nccl`` all-gathers the slices
-with NCCL and reassembles them instead (strong scaling either way).
+seeded synthetic data.  With N GPUs every rank runs the whole sweep on its
+own batch (data-parallel decode, weak scaling): these 7B layers fit one GPU
+many times over, and splitting them only adds latency to launches that are
+already latency-bound.
+
+Column-parallel sharding is measured where the benchmark configuration asks
+for it, on the Llama-3-70B MLP GEMMs of config 4 (the ``sharded`` object, at
+every N, N = 1 included): each rank holds N_layer / world output channels
+and runs its slice.  For decode (M = 1, 16), by default (``--exchange p2p``)
+the decode kernel sends its slice to every peer over NVLink as flagged words
+and unpacks theirs in the same launch (``rla_w8a16_gemm_allgather``);
+``--exchange nccl`` all-gathers the slices with NCCL instead.  The M = 4096
+prefill slice runs the tcgen05 kernel, then an NCCL all-gather (strong
+scaling).
 
 Reported (rank 0, one line):
   value      algorithmic bytes of the whole sweep (sum of N*K + 2MK + 2N + 2MN
-             over the 16 GEMMs) / device time per step, TB/s; steps replay a
-             CUDA graph of the step; device time is CUDA events on the replay
-             stream, max over ranks.
-  e2e        the same metric through the public API (``int8_gemm`` /
-             ``ColumnParallelInt8Linear``), eager, with every step's x copied
-             host->device from pinned memory and every y copied back.
+             over the 16 GEMMs), times the number of GPUs, / device time per
+             step, TB/s; steps replay a CUDA graph of the step; device time is
+             CUDA events on the replay stream, max over ranks.
+  e2e        the same metric through the public API (``Int8Linear``), eager,
+             with every step's x copied host->device from pinned memory and
+             every y copied back.
   roofline   the decode kernel: bytes per launch / its average launch time,
              against the measured HBM copy bandwidth.
   prefill    (N=1) the M=2048 prefill GEMMs of the benchmark configuration,
@@ -28,6 +36,8 @@ Reported (rank 0, one line):
              gate/up GEMM -> down) at M=8 (TB/s; 3 launches, SwiGLU in the
              decode kernel's epilogue) and M=2048 (TFLOP/s; 5 launches), next
              to the same block unfused (6 launches).
+  sharded    config 4: the 70B MLP GEMMs column-parallel over the N GPUs,
+             per shape and M, whole-job TB/s (decode) or TFLOP/s (M = 4096).
   cpu_baseline  the CPU oracle (rotalabs-accel's CPU algorithm restated in
              numpy) on one pass of the sweep, on this host's cores.
 
@@ -41,6 +51,7 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -54,6 +65,10 @@ DECODE_MS = (1, 4, 8, 16)
 DECODE_KN = ((4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336))
 PREFILL_M = 2048
 PREFILL_KN = ((4096, 12288), (4096, 11008), (11008, 4096))
+SHARDED_KN = ((8192, 28672), (28672, 8192))
+SHARDED_DECODE_M = (1, 16)
+SHARDED_PREFILL_M = 4096
+L2_BYTES = 126e6
 METRIC = "W8A16 GEMM achieved TB/s (decode M<=16) and TFLOPS (prefill M=2048) vs B200 roofline"
 
 
@@ -272,6 +287,77 @@ def measure_mlp_block(ra, _capi, dev, capture, timed, peaks, args):
     return out
 
 
+def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, args, exchange):
+    """Config 4: the Llama-3-70B MLP GEMMs (K=8192 -> N=28672, K=28672 ->
+    N=8192) column-parallel over the world's GPUs.  Each rank holds its
+    N / world output channels.  Decode (M = 1, 16): the fused peer-exchange
+    launch (``--exchange p2p``) or the local GEMM + NCCL all-gather + column
+    assembly (``--exchange nccl``); one GPU: the plain GEMM.  A decode step
+    runs the GEMM on several copies of the weight shard, together larger than
+    3 x L2, so nothing is re-read from L2.  Prefill (M = 4096): the local
+    tcgen05 GEMM, then the NCCL all-gather and assembly (one weight copy: the
+    GEMM is compute-bound).  Times are device-side, max over ranks; values are
+    whole-job (the full layer's algorithmic bytes or FLOPs / time)."""
+    import torch
+    from rotalabs_accel_b200.sharded import assemble_columns, shard_range
+    out = {"workload": "BASELINE config 4: Llama-3-70B MLP GEMMs (8192->28672, 28672->8192), M in {1, 16, 4096}, "
+                       f"column-parallel over {world} GPU(s); weights N(0, 0.02) per-channel int8, fp16 scales",
+           "exchange": ("none (one GPU)" if world == 1 else
+                        "decode: peer-to-peer all-gather fused into the decode kernel; prefill: NCCL all-gather"
+                        if exchange is not None else "NCCL all-gather + column assembly"),
+           "scaling": "strong"}
+    for (K, N) in SHARDED_KN:
+        start, stop, n_local = shard_range(N, world, rank)
+        copies = max(1, min(16, math.ceil(3 * L2_BYTES / (n_local * K))))
+        shards = []
+        for c in range(copies):
+            g = torch.Generator(device=dev).manual_seed(7000 + 31 * c + 1009 * rank + K)
+            q, sc = ra.quantize_weight_per_channel(torch.randn(n_local, K, generator=g, device=dev) * 0.02)
+            shards.append((q, sc.half()))
+        torch.cuda.synchronize()
+        for M in SHARDED_DECODE_M + (SHARDED_PREFILL_M,):
+            prefill = M == SHARDED_PREFILL_M
+            use = shards[:1] if prefill else shards
+            g = torch.Generator(device=dev).manual_seed(8000 + M + K)
+            x = torch.randn(M, K, generator=g, device=dev).half()
+            y = torch.empty(M, world * n_local, device=dev, dtype=torch.float16)
+            y_local = torch.empty(M, n_local, device=dev, dtype=torch.float16) if world > 1 else y
+            staging = torch.empty(world, M, n_local, device=dev, dtype=torch.float16) if world > 1 else None
+
+            def fn():
+                for (q, sc) in use:
+                    if world == 1:
+                        _capi.w8a16_gemm(x, q, sc, None, out=y)
+                    elif exchange is not None and not prefill:
+                        exchange.gemm(x, q, sc, None, out=y)
+                    else:
+                        _capi.w8a16_gemm(x, q, sc, None, out=y_local)
+                        dist.all_gather_into_tensor(staging, y_local)
+                        assemble_columns(staging, N, out=y)
+
+            steps = max(5, args.steps // 2000) if prefill else max(20, args.steps // 100)
+            gph = capture(fn)
+            ms, _ = timed(gph, steps, args.warmup)
+            del gph
+            ms_gemm = ms / len(use)
+            key = f"M={M} {K}->{N}"
+            if prefill:
+                tf = 2.0 * M * N * K / (ms_gemm * 1e-3) / 1e12
+                out[key] = {"us": round(ms_gemm * 1e3, 2), "value": round(tf, 1), "unit": "TFLOP/s",
+                            "frac": round(tf / (world * peaks["bf16_tflops"]), 4),
+                            "peak": f"{world} x dense bf16/fp16 burst ({peaks['source']})", "steps": steps}
+            else:
+                tbs = gemm_bytes(M, K, N) / (ms_gemm * 1e-3) / 1e12
+                out[key] = {"us": round(ms_gemm * 1e3, 2), "value": round(tbs, 3), "unit": "TB/s",
+                            "frac": round(tbs * 1e3 / (world * peaks["hbm_gbs"]), 4),
+                            "peak": f"{world} x HBM copy ({peaks['source']})", "weight_copies": len(use),
+                            "steps": steps}
+            del x, y, y_local, staging
+        del shards
+        torch.cuda.synchronize()
+    return out
+
+
 def run_case(case: str) -> int:
     """Small fixed workloads for profiler captures (no timing):
     ``sweep`` the 16 decode GEMMs once each; ``decode`` 4 launches of
@@ -342,7 +428,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
-                    help="N > 1: output exchange of the column-parallel layers")
+                    help="N > 1: output exchange of the column-parallel config 4 decode GEMMs")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the config 4 column-parallel measurement")
     ap.add_argument("--no-mlp", action="store_true", help="skip the config 3 MLP block measurement")
     ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "decode-large16", "skinny16", "prefill",
                                        "mlp8", "mlp2048"),
@@ -373,47 +460,32 @@ def main():
     import rotalabs_accel_b200 as ra
     from rotalabs_accel_b200 import _capi
     from rotalabs_accel_b200.peer import PeerExchange
-    from rotalabs_accel_b200.sharded import ColumnParallelInt8Linear, assemble_columns, shard_range
 
     peaks = load_peaks()
 
-    # ---- workload: every rank holds its column shard of every layer ----
+    # ---- workload: every rank runs the whole sweep on its own batch ----
+    # (the same weights on every rank, as replicas of one model; x differs)
     jobs = sweep()
     layers = []
     for i, (M, K, N) in enumerate(jobs):
         g = torch.Generator(device=dev).manual_seed(1000 + i)
-        x = torch.randn(M, K, generator=g, device=dev).half()
         w_full = torch.randn(N, K, generator=g, device=dev) * 0.02
-        start, stop, n_local = shard_range(N, world, rank)
-        q, s = ra.quantize_weight_per_channel(w_full[start:stop])
+        q, s = ra.quantize_weight_per_channel(w_full)
         del w_full
-        s = s.half()
-        y_local = torch.empty(M, n_local, device=dev, dtype=torch.float16)
-        staging = torch.empty(world, M, n_local, device=dev, dtype=torch.float16) if world > 1 else None
-        y = torch.empty(M, world * n_local, device=dev, dtype=torch.float16)
-        layers.append(dict(M=M, K=K, N=N, x=x, q=q, s=s, y_local=y_local, staging=staging, y=y, n_local=n_local))
+        gx = torch.Generator(device=dev).manual_seed(1000 + i + 100000 * rank)
+        x = torch.randn(M, K, generator=gx, device=dev).half()
+        y = torch.empty(M, N, device=dev, dtype=torch.float16)
+        layers.append(dict(M=M, K=K, N=N, x=x, q=q, s=s.half(), y=y))
     torch.cuda.synchronize()
     bytes_step = sum(gemm_bytes(M, K, N) for (M, K, N) in jobs)
     p2p = world > 1 and args.exchange == "p2p"
-    exchange = PeerExchange(max_rows=max(L["M"] for L in layers),
-                            max_n_local=max(L["n_local"] for L in layers)) if p2p else None
+    exchange = None
 
     stream = torch.cuda.Stream(device=dev)
 
-    def gemm_only():
-        for L in layers:
-            _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y_local"] if world > 1 else L["y"])
-
     def step():
         for L in layers:
-            if world == 1:
-                _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y"])
-            elif p2p:
-                exchange.gemm(L["x"], L["q"], L["s"], None, out=L["y"])
-            else:
-                _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y_local"])
-                dist.all_gather_into_tensor(L["staging"], L["y_local"])
-                assemble_columns(L["staging"], L["N"], out=L["y"])
+            _capi.w8a16_gemm(L["x"], L["q"], L["s"], None, out=L["y"])
 
     def capture(fn):
         with torch.cuda.stream(stream):
@@ -456,25 +528,16 @@ def main():
             ms = t.item()
         return ms, clocks
 
-    launches_per_step = len(layers)   # one GEMM kernel per layer (the fused exchange included)
-    if world > 1 and not p2p:
-        launches_per_step = len(layers) + sum(1 for L in layers if L["M"] > 1)   # + gather kernel (M=1: a copy)
+    launches_per_step = len(layers) * world   # one GEMM kernel per layer on every GPU
 
     g_step = capture(step)
     ms_step, clocks = timed(g_step, args.steps, args.warmup, sample_clocks=(rank == 0))
-    value = bytes_step / (ms_step * 1e-3) / 1e12
+    value = world * bytes_step / (ms_step * 1e-3) / 1e12
 
-    # ---- the decode kernel alone (roofline) ----
-    if world == 1:
-        ms_gemm = ms_step
-        g_gemm = None
-    else:
-        g_gemm = capture(gemm_only)
-        ms_gemm, _ = timed(g_gemm, max(100, args.steps // 4), args.warmup)
-    local_bytes = sum(gemm_bytes(L["M"], L["K"], L["n_local"]) for L in layers)
-    avg_launch_us = ms_gemm * 1e3 / len(layers)
-    achieved = local_bytes / len(layers) / (avg_launch_us * 1e-6) / 1e9
-    traffic = load_traffic() if world == 1 else None
+    # ---- the decode kernel (roofline): every launch of the step is one ----
+    avg_launch_us = ms_step * 1e3 / len(layers)
+    achieved = bytes_step / len(layers) / (avg_launch_us * 1e-6) / 1e9
+    traffic = load_traffic()
 
     # ---- end to end through the public API, host buffers ----
     torch.cuda.synchronize()
@@ -482,19 +545,11 @@ def main():
     ys_host = [torch.empty(L["M"], L["N"], dtype=torch.float16).pin_memory() for L in layers]
     mods = []
     for L in layers:
-        if world > 1:
-            m = ColumnParallelInt8Linear(L["K"], L["N"]).to(dev)
-            m.weight_int8.copy_(L["q"])
-            m.scale.copy_(L["s"].float())
-            m._quantized = True
-            if p2p:
-                m.enable_peer_exchange(max_tokens=L["M"], exchange=exchange)
-        else:
-            m = ra.Int8Linear(L["K"], L["N"])
-            m.weight_int8 = L["q"]
-            m.scale = L["s"]
-            m.weight_transposed = torch.empty(0, dtype=torch.int8, device=dev)
-            m._quantized = True
+        m = ra.Int8Linear(L["K"], L["N"])
+        m.weight_int8 = L["q"]
+        m.scale = L["s"]
+        m.weight_transposed = torch.empty(0, dtype=torch.int8, device=dev)
+        m._quantized = True
         mods.append(m)
     h2d = sum(t.numel() * 2 for t in xs_host)
     d2h = sum(t.numel() * 2 for t in ys_host)
@@ -541,7 +596,7 @@ def main():
         t = torch.tensor([ms_e2e], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_e2e = t.item()
-    e2e_value = bytes_step / (ms_e2e * 1e-3) / 1e12
+    e2e_value = world * bytes_step / (ms_e2e * 1e-3) / 1e12
 
     # ---- prefill (N = 1) ----
     prefill = None
@@ -574,6 +629,13 @@ def main():
     if world == 1 and not args.no_mlp:
         mlp_block = measure_mlp_block(ra, _capi, dev, capture, timed, peaks, args)
 
+    # ---- config 4: the 70B MLP GEMMs, column-parallel over the GPUs ----
+    sharded = None
+    if not args.no_sharded:
+        exchange = PeerExchange(max_rows=max(SHARDED_DECODE_M),
+                                max_n_local=max(-(-N // world) for (_, N) in SHARDED_KN)) if p2p else None
+        sharded = measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, args, exchange)
+
     # ---- CPU baseline (rank 0, N = 1) ----
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -590,15 +652,14 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp16 (int8 weights, fp32 accumulate)",
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (int8 weights, fp32 accumulate)",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) per-channel int8 weights)",
             "config": {"workload": "decode GEMV sweep, BASELINE config 1: M in {1,4,8,16} x (K,N) in "
                                    "{(4096,4096),(4096,11008),(11008,4096),(4096,14336)}, 16 GEMMs per step",
                        "parallelism": "single GPU" if world == 1 else
-                       (f"column-parallel over {world} GPUs, peer-to-peer all-gather fused into the decode kernel "
-                        "(flagged-word stores over NVLink, unpacked in the same launch)" if p2p else
-                        f"column-parallel over {world} GPUs + NCCL all-gather of each output"),
-                       "weights_bytes": sum(L["q"].numel() for L in layers) * world,
+                       f"{world} replicas (data-parallel decode: every GPU runs the whole sweep on its own batch, "
+                       "no collective); column-parallel sharding is measured on config 4 (the sharded object)",
+                       "weights_bytes_per_gpu": sum(L["q"].numel() for L in layers),
                        "l2": "working set > L2: each GEMM has its own weight (663 MB total), no L2 reuse",
                        "timing": "CUDA graph of one step, K replays between CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -612,7 +673,7 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
                     "path": "Int8Linear.forward (public API), eager; per step one pinned host -> device copy "
                             "of all 16 inputs, and all 16 outputs read back in one device -> pinned host copy"
-                    if world == 1 else "ColumnParallelInt8Linear.forward, eager, pinned host buffers"},
+                            + ("" if world == 1 else "; on every GPU, max over ranks")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -621,13 +682,11 @@ def main():
             line["prefill"] = prefill
         if mlp_block:
             line["mlp_block"] = mlp_block
-        if world > 1:
-            line["gemm_only_ms_per_step"] = round(ms_gemm, 5)
+        if sharded:
+            line["sharded"] = sharded
         print(json.dumps(line), flush=True)
 
     del g_step
-    if g_gemm is not None:
-        del g_gemm
     torch.cuda.synchronize()
     if exchange is not None:
         exchange.close()
