@@ -45,7 +45,8 @@ int device_sm_count() {
 // tcgen05 kernel (M > 32): tile 128 weight rows x BM tokens; BM = 256 for
 // long prefills, smaller for mid-size M so that the grid covers the SMs.
 // ---------------------------------------------------------------------------
-static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws, int sms, bool gated = false) {
+static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws, int sms, bool gated = false,
+                         bool peer = false) {
   p.kernel = RLA_KERNEL_SKINNY;
   p.nt = M <= 8 ? 1 : M <= 16 ? 2 : 4;
   const int64_t chunks = (K + 63) / 64;
@@ -65,7 +66,7 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   // M = 1, 688 CTAs, 15.7 -> 11.1 us; 4096 -> 14336 at M = 1, 896 CTAs,
   // 16.4 -> 12.1 us; the gated 4096 -> 2 x 11008 at M = 16, 1376 CTAs (more
   // than one wave either way), 34.8 -> 28.3 us.
-  if (p.wn == 1 && p.wk == 8 && p.grid_x > (int64_t)skinny_ctas_per_sm(p.nt, 1, 8, gated) * sms)
+  if (p.wn == 1 && p.wk == 8 && p.grid_x > (int64_t)skinny_ctas_per_sm(p.nt, 1, 8, gated, false, peer) * sms)
     p.wk = 4;
   // M = 9..16 in 128-thread CTAs: loading each chunk's activations just
   // before its MMAs costs registers (fewer CTAs fit per SM) but streams
@@ -74,7 +75,7 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   // more than fit) would need a second wave: 26.2 us against 18.6 without.
   p.xjit = 0;
   if (p.nt == 2 && p.wn == 1 && p.wk == 4 && !gated &&
-      p.grid_x <= (int64_t)skinny_ctas_per_sm(p.nt, 1, 4, false, true) * sms)
+      p.grid_x <= (int64_t)skinny_ctas_per_sm(p.nt, 1, 4, false, true, peer) * sms)
     p.xjit = 1;
   p.splits = 1;
   p.cluster = 0;
@@ -82,7 +83,7 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   // measured on B200, a second wave costs more than the extra parallelism
   // gains (e.g. 4096 x 4096 at M = 16: 7.7 us unsplit vs 10.9 us with two
   // slices at two resident CTAs per SM; at M = 1, four per SM, two slices win).
-  const int64_t resident = (int64_t)skinny_ctas_per_sm(p.nt, p.wn, p.wk, gated, p.xjit != 0) * sms;
+  const int64_t resident = (int64_t)skinny_ctas_per_sm(p.nt, p.wn, p.wk, gated, p.xjit != 0, peer) * sms;
   if (p.grid_x < resident) {
     // Each CTA slice should still give every k-warp a few chunks.
     const int64_t max_splits = chunks / (2 * p.wk);
@@ -123,7 +124,7 @@ static void stream_shape(Plan& p, int64_t M, int64_t N, int64_t K, int sms) {
   p.workspace = stream_workspace_bytes(M, p.grid_x);
 }
 
-Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace) {
+Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace, bool peer) {
   Plan p;
   if (M == 0 || N == 0) return p;
   if (K == 0) {
@@ -134,7 +135,7 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
   if (aligned && K % 16 == 0 && M <= 32) {
     const int choice = g_decode_kernel.load(std::memory_order_relaxed);
     Plan sk;
-    skinny_shape(sk, M, N, K, have_workspace, sms);
+    skinny_shape(sk, M, N, K, have_workspace, sms, false, peer);
     // Measured on B200 (CUDA graphs of back-to-back launches): the persistent
     // stream-K kernel wins on weights of 120 MB or more, and from M = 9 on
     // weights of 40 MB or more when the skinny grid needs more than one wave
@@ -143,7 +144,8 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
     // The skinny kernel wins on smaller layers and on narrow column shards
     // (lower fixed cost per launch).
     const double wbytes = static_cast<double>(N) * static_cast<double>(K);
-    const bool multi_wave = sk.grid_x > (int64_t)skinny_ctas_per_sm(sk.nt, sk.wn, sk.wk, false, sk.xjit != 0) * sms;
+    const bool multi_wave =
+        sk.grid_x > (int64_t)skinny_ctas_per_sm(sk.nt, sk.wn, sk.wk, false, sk.xjit != 0, peer) * sms;
     const bool stream_wins = M <= 16 && ((M > 8 && wbytes >= 40e6 && multi_wave) || wbytes >= 120e6);
     const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
     // The stream kernel keeps one arrival counter per CTA in the counter region.

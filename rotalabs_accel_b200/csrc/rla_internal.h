@@ -84,7 +84,8 @@ constexpr int kMaxSplitRowBlocks = static_cast<int>(kSplitCounterBytes / sizeof(
 // Largest split-K done inside one thread-block cluster (the portable cluster size).
 constexpr int kMaxClusterSplits = 8;
 
-Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace);
+// peer: plan for the launch with the fused peer exchange (its own occupancy)
+Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace, bool peer = false);
 
 void note_launch();
 int device_sm_count();  // SMs of the current device (148 if it cannot be read)
@@ -93,7 +94,7 @@ void set_error(const char* fmt, ...);
 cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
 // Resident CTAs per SM of the skinny kernel instance (plain or gated form);
 // 2 when the device cannot be queried.
-int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit = false);
+int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit = false, bool peer = false);
 cudaError_t launch_stream(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
 size_t stream_workspace_bytes(int64_t M, int ctas);
 size_t stream_smem_bytes(int nt);

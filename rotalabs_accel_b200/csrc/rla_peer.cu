@@ -162,8 +162,10 @@ int rla_w8a16_gemm_allgather(const void* x, int64_t ldx, const int8_t* w, int64_
               recv_bytes, world, (long long)slot_words);
     return RLA_ERR_WORKSPACE;
   }
-  Plan p = make_plan(M, n_local, K, true, workspace != nullptr && workspace_bytes > 0);
-  if (p.workspace > workspace_bytes) p = make_plan(M, n_local, K, true, false);
+  // planned with the exchange kernel's own occupancy (it holds more
+  // registers than the plain kernel, so fewer of its CTAs fit per SM)
+  Plan p = make_plan(M, n_local, K, true, workspace != nullptr && workspace_bytes > 0, /*peer=*/true);
+  if (p.workspace > workspace_bytes) p = make_plan(M, n_local, K, true, false, /*peer=*/true);
   if (p.kernel != RLA_KERNEL_SKINNY && p.kernel != RLA_KERNEL_STREAM) {
     set_error("rla_w8a16_gemm_allgather: the plan for this shape is not a decode kernel");
     return RLA_ERR_UNSUPPORTED;

@@ -440,18 +440,22 @@ static cudaError_t launch_nt(const GemmArgs& a, const Plan& p, void* ws, cudaStr
   return cudaErrorInvalidConfiguration;
 }
 
+// Resident CTAs per SM of one instantiation: form 0 plain, 1 gated (GLU),
+// 2 with the peer exchange (PEER).  Queried once per form and cached.
 template <int NT, int WN, int WK, bool XJ>
-static int ctas_per_sm_cfg(bool gated) {
+static int ctas_per_sm_cfg(int form) {
   constexpr int U = NT >= 4 ? 2 : 4;
-  static int cache[2] = {-1, -1};
-  int& c = cache[gated ? 1 : 0];
+  static int cache[3] = {-1, -1, -1};
+  int& c = cache[form];
   if (c < 0) {
     int v = 0;
     const cudaError_t e =
-        gated ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                    &v, w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>, 32 * WN * WK, 0)
-              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                    &v, w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>, 32 * WN * WK, 0);
+        form == 1   ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                        &v, w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>, 32 * WN * WK, 0)
+        : form == 2 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                          &v, w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>, 32 * WN * WK, 0)
+                    : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                          &v, w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>, 32 * WN * WK, 0);
     if (e != cudaSuccess || v < 1) {
       (void)cudaGetLastError();
       return 2;   // no device to ask (e.g. planning on a CPU-only host)
@@ -462,24 +466,25 @@ static int ctas_per_sm_cfg(bool gated) {
 }
 
 template <int NT>
-static int ctas_per_sm_nt(int wn, int wk, bool gated, bool xjit) {
-  if (wn == 1 && wk == 8) return ctas_per_sm_cfg<NT, 1, 8, NT == 1>(gated);
-  if (wn == 2 && wk == 4) return ctas_per_sm_cfg<NT, 2, 4, false>(gated);
-  if (wn == 4 && wk == 2) return ctas_per_sm_cfg<NT, 4, 2, false>(gated);
+static int ctas_per_sm_nt(int wn, int wk, int form, bool xjit) {
+  if (wn == 1 && wk == 8) return ctas_per_sm_cfg<NT, 1, 8, NT == 1>(form);
+  if (wn == 2 && wk == 4) return ctas_per_sm_cfg<NT, 2, 4, false>(form);
+  if (wn == 4 && wk == 2) return ctas_per_sm_cfg<NT, 4, 2, false>(form);
   if (wn == 1 && wk == 4) {
     if constexpr (NT == 2) {
-      if (xjit) return ctas_per_sm_cfg<NT, 1, 4, true>(gated);
+      if (xjit) return ctas_per_sm_cfg<NT, 1, 4, true>(form);
     }
-    return ctas_per_sm_cfg<NT, 1, 4, false>(gated);
+    return ctas_per_sm_cfg<NT, 1, 4, false>(form);
   }
   return 2;
 }
 
-int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit) {
+int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit, bool peer) {
+  const int form = gated ? 1 : peer ? 2 : 0;
   switch (nt) {
-    case 1: return ctas_per_sm_nt<1>(wn, wk, gated, xjit);
-    case 2: return ctas_per_sm_nt<2>(wn, wk, gated, xjit);
-    case 4: return ctas_per_sm_nt<4>(wn, wk, gated, xjit);
+    case 1: return ctas_per_sm_nt<1>(wn, wk, form, xjit);
+    case 2: return ctas_per_sm_nt<2>(wn, wk, form, xjit);
+    case 4: return ctas_per_sm_nt<4>(wn, wk, form, xjit);
     default: return 2;
   }
 }
