@@ -146,7 +146,15 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
     const double wbytes = static_cast<double>(N) * static_cast<double>(K);
     const bool multi_wave =
         sk.grid_x > (int64_t)skinny_ctas_per_sm(sk.nt, sk.wn, sk.wk, false, sk.xjit != 0, peer) * sms;
-    const bool stream_wins = M <= 16 && ((M > 8 && wbytes >= 40e6 && multi_wave) || wbytes >= 120e6);
+    // With the fused peer exchange the skinny kernel's exchange form holds
+    // many more registers and loses more (one GPU, world-1 exchange, M = 16:
+    // 8192 -> 14336 skinny 75.9 us vs stream 36.4; 28672 -> 4096 60.8 vs 37.8;
+    // 8192 -> 3584 18.8 vs 18.5; M = 1: 8192 -> 14336 38.2 vs 30.5,
+    // 28672 -> 4096 29.4 vs 31.4), while the stream kernel's exchange costs
+    // about 2 us over its plain launch.
+    const bool stream_wins =
+        M <= 16 && (peer ? ((M > 8 && wbytes >= 25e6) || wbytes >= 100e6)
+                         : ((M > 8 && wbytes >= 40e6 && multi_wave) || wbytes >= 120e6));
     const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
     // The stream kernel keeps one arrival counter per CTA in the counter region.
     if (have_workspace && want_stream && sms <= kMaxSplitRowBlocks) {
