@@ -184,7 +184,9 @@ RLA_API int rla_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, 
  * holds all slices: no gather, no reorder, no host synchronisation.
  *
  *   x, ldx, w (int8 [n_local, K], row stride ldw), scale, bias, workspace:
- *          as in rla_w8a16_gemm, with N = n_local.
+ *          as in rla_w8a16_gemm, with N = n_local; size the workspace with
+ *          rla_w8a16_allgather_workspace_size (this launch is planned for
+ *          the exchange kernel, which can differ from rla_w8a16_gemm's plan).
  *   y      this rank's fp16 output [M, ldy], ldy >= world * n_local (any
  *          device memory; not shared with the peers).
  *   recv_peers  HOST array of `world` device pointers, valid in this process,
@@ -214,6 +216,10 @@ RLA_API int rla_w8a16_gemm_allgather(const void* x, int64_t ldx, const int8_t* w
                                      int64_t M, int64_t n_local, int64_t K, void* const* recv_peers,
                                      size_t recv_bytes, void* sync, int rank, int world, void* workspace,
                                      size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace the plan of rla_w8a16_gemm_allgather for (M, n_local, K)
+ * can use (0 if none).  Part of the same replacement as that entry point. */
+RLA_API size_t rla_w8a16_allgather_workspace_size(int64_t M, int64_t n_local, int64_t K);
 
 /* Limit of every wait inside rla_w8a16_gemm_allgather, in nanoseconds
  * (default 1 s; 1 ms .. 60 s).  Process-wide. */

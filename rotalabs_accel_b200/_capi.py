@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "rla_set_decode_kernel", "rla_w8a16_gemm_allgather", "rla_set_peer_wait_limit", "rla_peer_alloc",
     "rla_peer_free", "rla_ipc_export", "rla_ipc_open", "rla_ipc_close",
     "rla_w8a16_gemm_swiglu", "rla_w8a16_swiglu_workspace_size", "rla_rmsnorm",
+    "rla_w8a16_allgather_workspace_size",
 )
 
 MAX_PEERS = 8
@@ -107,6 +108,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.rla_w8a16_swiglu_workspace_size.restype = sz
         lib.rla_rmsnorm.argtypes = [p, i64, p, ctypes.c_int, ctypes.c_float, p, i64, i64, i64, p]
         lib.rla_rmsnorm.restype = ctypes.c_int
+        lib.rla_w8a16_allgather_workspace_size.argtypes = [i64, i64, i64]
+        lib.rla_w8a16_allgather_workspace_size.restype = sz
         if os.path.abspath(path) == LIB_PATH:
             # linked to this library by soname: the loader reuses the copy
             # loaded above, so both bindings share one library state
@@ -313,7 +316,7 @@ def w8a16_gemm_allgather(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: to
     world = len(recv_ptrs)
     recv = (ctypes.c_void_p * world)(*recv_ptrs)
     stream = torch.cuda.current_stream(x2d.device).cuda_stream
-    need = lib.rla_w8a16_workspace_size(M, n_local, K)
+    need = lib.rla_w8a16_allgather_workspace_size(M, n_local, K)
     ws_ptr, ws_bytes = None, 0
     if need:
         ws = _workspace(x2d.device, stream, need)

@@ -103,6 +103,12 @@ int rla_ipc_close(void* ptr) {
   return RLA_OK;
 }
 
+size_t rla_w8a16_allgather_workspace_size(int64_t M, int64_t n_local, int64_t K) {
+  using namespace rla;
+  if (M < 0 || n_local < 0 || K < 0) return 0;
+  return make_plan(M, n_local, K, true, true, /*peer=*/true).workspace;
+}
+
 int rla_w8a16_gemm_allgather(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
                              int scale_dtype, const void* bias, int bias_dtype, void* y, int64_t ldy, int64_t M,
                              int64_t n_local, int64_t K, void* const* recv_peers, size_t recv_bytes, void* sync,

@@ -170,3 +170,14 @@ def test_fast_call_bindings_share_the_library():
     maps = open("/proc/self/maps").read()
     paths = {line.split()[-1] for line in maps.splitlines() if line.endswith("librla_w8a16.so")}
     assert len(paths) == 1, paths
+
+
+def test_allgather_workspace_size():
+    """The fused-exchange launch is planned for its own kernel form: for a
+    70B shard at M = 16 it takes the stream kernel, whose workspace the
+    exchange query reports; sizes are multiples of 4 and 0 for empty shapes."""
+    lib = _capi.load_library()
+    need = lib.rla_w8a16_allgather_workspace_size(16, 14336, 8192)
+    assert need > 4096 and need % 4 == 0
+    assert lib.rla_w8a16_allgather_workspace_size(0, 14336, 8192) == 0
+    assert lib.rla_w8a16_allgather_workspace_size(-1, 14336, 8192) == 0
