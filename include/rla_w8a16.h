@@ -205,11 +205,18 @@ RLA_API int rla_w8a16_gemm_noalloc(const void* x, int64_t ldx, const int8_t* w, 
  * launched, and the caller uses its collective path.  Waits are bounded
  * (rla_set_peer_wait_limit); a wait that gives up records device error 7 (a
  * peer's slice did not arrive) or 8 (this launch's CTAs did not all finish)
- * and leaves y incomplete; after that, free and re-create the buffers on
- * every rank.  Stores to peers are plain stores over NVLink (no multicast).
+ * and leaves y incomplete.  The sync area then stays marked: every later call
+ * on it records device error 9 and returns at once with y incomplete (no
+ * second wait of the full limit).  After device error 7, 8 or 9, every rank
+ * frees and re-creates its buffers and sync area (receive buffers may still
+ * hold words of the failed call).  Stores to peers are plain stores over
+ * NVLink (no multicast).
  */
 #define RLA_MAX_PEERS 8
 #define RLA_PEER_SYNC_BYTES 512
+/* Index (in 32-bit words) of the sync area's abort word: non-zero once a wait
+ * of an exchange call on that sync area has given up (a host may read it). */
+#define RLA_PEER_SYNC_ABORT_WORD 96
 #define RLA_IPC_HANDLE_BYTES 64
 RLA_API int rla_w8a16_gemm_allgather(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scale,
                                      int scale_dtype, const void* bias, int bias_dtype, void* y, int64_t ldy,

@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
 
 MAX_PEERS = 8
 PEER_SYNC_BYTES = 512
+PEER_SYNC_ABORT_WORD = 96
 IPC_HANDLE_BYTES = 64
 
 _lib = None

@@ -26,6 +26,15 @@ void set_error(const char* fmt, ...) {
 
 static constexpr int kNumSMs = 148;  // B200; refined from the device at run time
 
+#ifdef RLA_EXPERIMENTS
+// Experiment builds only (never the shipped library): plan overrides from the
+// environment, for A/B timing of plan rules.
+static int exp_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v && *v ? atoi(v) : dflt;
+}
+#endif
+
 int device_sm_count() {
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kNumSMs;
@@ -68,6 +77,11 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   // than one wave either way), 34.8 -> 28.3 us.
   if (p.wn == 1 && p.wk == 8 && p.grid_x > (int64_t)skinny_ctas_per_sm(p.nt, 1, 8, gated, false, peer) * sms)
     p.wk = 4;
+  // Long K at M <= 8: 128-thread CTAs with twice the K slices.  Measured on
+  // B200 at M = 1: 28672 -> 8192 49.8 -> 39.0 us, 28672 -> 1024 9.8 -> 8.5 us,
+  // 8192 -> 3584 9.1 -> 8.2 us; not at 11008 -> 4096 (12.0 -> 12.6 us).
+  if (!gated && !peer && p.nt == 1 && p.wn == 1 && p.wk == 8 && (K >= 16384 || (K >= 8192 && N < 4096)))
+    p.wk = 4;
   // M = 9..16 in 128-thread CTAs: loading each chunk's activations just
   // before its MMAs costs registers (fewer CTAs fit per SM) but streams
   // faster; used while the grid still fits in one wave.  Measured on B200,
@@ -77,25 +91,49 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   if (p.nt == 2 && p.wn == 1 && p.wk == 4 && !gated &&
       p.grid_x <= (int64_t)skinny_ctas_per_sm(p.nt, 1, 4, false, true, peer) * sms)
     p.xjit = 1;
+#ifdef RLA_EXPERIMENTS
+  {
+    const int ewk = exp_int("RLA_EXP_WK", 0);
+    if (p.wn == 1 && (ewk == 4 || ewk == 8)) {
+      p.wk = ewk;
+      if (ewk == 8) p.xjit = 0;
+    }
+  }
+#endif
   p.splits = 1;
   p.cluster = 0;
   // Split K only as far as the whole grid stays resident at once (one wave):
   // measured on B200, a second wave costs more than the extra parallelism
   // gains (e.g. 4096 x 4096 at M = 16: 7.7 us unsplit vs 10.9 us with two
   // slices at two resident CTAs per SM; at M = 1, four per SM, two slices win).
-  const int64_t resident = (int64_t)skinny_ctas_per_sm(p.nt, p.wn, p.wk, gated, p.xjit != 0, peer) * sms;
+  const int64_t resident = skinny_resident_ctas(p.nt, p.wn, p.wk, gated, p.xjit != 0, peer, 1);
   if (p.grid_x < resident) {
     // Each CTA slice should still give every k-warp a few chunks.
     const int64_t max_splits = chunks / (2 * p.wk);
     int64_t s = resident / p.grid_x;
     if (s > max_splits) s = max_splits;
     if (s > 32) s = 32;
+#ifdef RLA_EXPERIMENTS
+    {
+      const int ems = exp_int("RLA_EXP_MAXSPLIT", 0);
+      if (ems > 0 && s > ems) s = ems;
+    }
+#endif
     if (s > 1) {
       if (s <= kMaxClusterSplits || !have_ws || p.grid_x > kMaxSplitRowBlocks) {
         // the slices of a row block are one thread-block cluster and add up
         // through distributed shared memory: no workspace, no global round trip
-        p.splits = static_cast<int>(s < kMaxClusterSplits ? s : kMaxClusterSplits);
-        p.cluster = 1;
+        s = s < kMaxClusterSplits ? s : kMaxClusterSplits;
+        // The whole grid must still fit at once counted in whole clusters
+        // (all CTAs of a cluster sit in one GPC), which can be fewer CTAs
+        // than the per-SM count suggests.
+        while (s > 1 && p.grid_x * s > (int64_t)skinny_resident_ctas(p.nt, p.wn, p.wk, gated, p.xjit != 0, peer,
+                                                                     static_cast<int>(s)))
+          --s;
+        if (s > 1) {
+          p.splits = static_cast<int>(s);
+          p.cluster = 1;
+        }
       } else {
         p.splits = static_cast<int>(s);  // fp32 partial sums in the workspace
       }
@@ -136,13 +174,12 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
     const int choice = g_decode_kernel.load(std::memory_order_relaxed);
     Plan sk;
     skinny_shape(sk, M, N, K, have_workspace, sms, false, peer);
-    // Measured on B200 (CUDA graphs of back-to-back launches): the persistent
-    // stream-K kernel wins on weights of 120 MB or more, and from M = 9 on
+    // Measured on B200 (CUDA graphs of back-to-back launches): from M = 9 on,
+    // the persistent stream-K kernel wins on weights of 120 MB or more, and on
     // weights of 40 MB or more when the skinny grid needs more than one wave
-    // of resident CTAs (e.g. M = 16: 4096 -> 11008 stream 18.9 us vs skinny
-    // 21.0 us; 11008 -> 4096, one skinny wave, skinny 18.4 us vs 20.5 us).
-    // The skinny kernel wins on smaller layers and on narrow column shards
-    // (lower fixed cost per launch).
+    // of resident CTAs.  The skinny kernel wins on smaller layers, on narrow
+    // column shards (lower fixed cost per launch) and, for M <= 8, on large
+    // layers too.
     const double wbytes = static_cast<double>(N) * static_cast<double>(K);
     const bool multi_wave =
         sk.grid_x > (int64_t)skinny_ctas_per_sm(sk.nt, sk.wn, sk.wk, false, sk.xjit != 0, peer) * sms;
@@ -152,9 +189,12 @@ Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspac
     // 8192 -> 3584 18.8 vs 18.5; M = 1: 8192 -> 14336 38.2 vs 30.5,
     // 28672 -> 4096 29.4 vs 31.4), while the stream kernel's exchange costs
     // about 2 us over its plain launch.
+    // For M <= 8 the skinny kernel now wins on large layers too (M = 1:
+    // 8192 -> 28672 skinny 40.9 us vs stream 45.2; 28672 -> 8192 39.0 vs
+    // 45.3); at M = 16 the stream kernel keeps them (55.9 vs 64.9 us).
     const bool stream_wins =
         M <= 16 && (peer ? ((M > 8 && wbytes >= 25e6) || wbytes >= 100e6)
-                         : ((M > 8 && wbytes >= 40e6 && multi_wave) || wbytes >= 120e6));
+                         : (M > 8 && ((wbytes >= 40e6 && multi_wave) || wbytes >= 120e6)));
     const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
     // The stream kernel keeps one arrival counter per CTA in the counter region.
     if (have_workspace && want_stream && sms <= kMaxSplitRowBlocks) {

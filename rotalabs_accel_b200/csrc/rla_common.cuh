@@ -28,6 +28,7 @@ enum : unsigned int {
   RLA_DEVERR_TIMEOUT_SPLITK = 6,
   RLA_DEVERR_TIMEOUT_PEER_DATA = 7,  // a peer's slice of an exchange call did not arrive
   RLA_DEVERR_TIMEOUT_GRID = 8,       // CTAs of an exchange launch did not all finish their slice
+  RLA_DEVERR_PEER_POISONED = 9,      // an exchange call on a sync area whose earlier wait gave up
 };
 
 // One second: far above any legitimate wait inside one launch.
@@ -40,6 +41,11 @@ RLA_DEVFN uint64_t rla_globaltimer() {
 }
 
 RLA_DEVFN void rla_record_error(unsigned int code) { atomicCAS(&rla_device_error, 0u, code); }
+
+// Before a <<<...>>> launch whose status is read with cudaGetLastError():
+// drop a non-sticky error left by an earlier failed call (already returned to
+// that call's caller), so the status read after the launch is this launch's.
+static inline void rla_clear_stale_launch_error() { (void)cudaGetLastError(); }
 
 // Split-K / stream-K arrival: one acquire-release atomic at gpu scope.  The
 // release publishes every store the caller's CTA made before its barrier
@@ -128,6 +134,9 @@ RLA_DEVFN void rla_griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "mem
 RLA_DEVFN void rla_griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // Pull the cache line holding `p` into L2 (never stale: L2 is coherent).
 RLA_DEVFN void rla_prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+// Pull the cache line holding `p` into this SM's L1.  Only for data that no
+// kernel running at the same time writes (here: after the dependency wait).
+RLA_DEVFN void rla_prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
 
 // ---------------------------------------------------------------------------
 // Thread-block clusters: rank, barrier, distributed shared memory.

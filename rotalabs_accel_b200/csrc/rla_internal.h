@@ -18,8 +18,9 @@ constexpr int kMaxPeers = 8;
 constexpr int kSyncSeq = 0;        // exchange calls this rank has completed
 constexpr int kSyncArrive = 32;    // CTAs of the running call that finished phase 1
 constexpr int kSyncUnpacked = 64;  // unpacking CTAs of the running call that are done
-constexpr int kSyncAbort = 96;     // call number whose wait gave up (stops the other waits)
+constexpr int kSyncAbort = 96;     // call number whose wait gave up (stops the other waits; never cleared)
 constexpr size_t kSyncBytes = 512;
+static_assert(kSyncAbort == RLA_PEER_SYNC_ABORT_WORD && kSyncBytes == RLA_PEER_SYNC_BYTES, "sync area layout");
 
 struct PeerOut {
   uint2* recv[kMaxPeers];       // rank d's receive buffer: 2 halves (call parity) of flagged words
@@ -95,6 +96,10 @@ cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cud
 // Resident CTAs per SM of the skinny kernel instance (plain or gated form);
 // 2 when the device cannot be queried.
 int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit = false, bool peer = false);
+// CTAs of the skinny kernel instance that fit on the device at once, with the
+// K slices of a row block in clusters of `cluster` CTAs (whole clusters
+// counted); 2 per SM when the device cannot be queried.
+int skinny_resident_ctas(int nt, int wn, int wk, bool gated, bool xjit, bool peer, int cluster);
 cudaError_t launch_stream(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s);
 size_t stream_workspace_bytes(int64_t M, int ctas);
 size_t stream_smem_bytes(int nt);

@@ -84,6 +84,7 @@ cudaError_t launch_generic(const GemmArgs& a, cudaStream_t s) {
   const int64_t blocks = (warps * 32 + 255) / 256;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   auto kern = a.w_up ? w8a16_generic_kernel<true> : w8a16_generic_kernel<false>;
+  rla_clear_stale_launch_error();
   kern<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __half*>(a.x), a.ldx, a.w, a.ldw, a.scale, a.scale_f32,
                                         a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K,
                                         a.w_up, a.scale_up, a.bias_up);
@@ -126,6 +127,7 @@ cudaError_t launch_swiglu(const void* gate, const void* up, int64_t ld, void* y,
                    (reinterpret_cast<uintptr_t>(up) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
   const int64_t work = (vec ? (int64_t)N / 8 : (int64_t)N) * M;
   const int64_t blocks = std::min<int64_t>((work + 255) / 256, 148 * 16);
+  rla_clear_stale_launch_error();
   swiglu_rows_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(
       static_cast<const __half*>(gate), static_cast<const __half*>(up), ld, static_cast<__half*>(y), ldy, M, N,
       vec ? 1 : 0);
@@ -237,6 +239,7 @@ __global__ void w8a16_fill_kernel(const void* __restrict__ bias, int bias_kind, 
 
 cudaError_t launch_fill(const GemmArgs& a, cudaStream_t s) {
   const int64_t total = static_cast<int64_t>(a.M) * a.N;
+  rla_clear_stale_launch_error();
   w8a16_fill_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(a.bias, a.bias_kind,
                                                                      static_cast<__half*>(a.y), a.ldy, a.M, a.N);
   return cudaGetLastError();
@@ -306,12 +309,15 @@ cudaError_t launch_quantize(const void* w, int w_dtype, int64_t ldw, int64_t N, 
   const unsigned blocks = static_cast<unsigned>(N);
   switch (w_dtype) {
     case RLA_DTYPE_F32:
+      rla_clear_stale_launch_error();
       quantize_rows_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(w), ldw, (int)K, q, ldq, scale);
       break;
     case RLA_DTYPE_F16:
+      rla_clear_stale_launch_error();
       quantize_rows_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(w), ldw, (int)K, q, ldq, scale);
       break;
     case RLA_DTYPE_BF16:
+      rla_clear_stale_launch_error();
       quantize_rows_kernel<__nv_bfloat16>
           <<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(w), ldw, (int)K, q, ldq, scale);
       break;
@@ -356,6 +362,7 @@ cudaError_t launch_gather(const void* staging, int64_t world, int64_t M, int64_t
   int64_t blocks = (elems + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
+  rla_clear_stale_launch_error();
   if (vec)
     gather_columns_vec_kernel<<<(unsigned)blocks, 256, 0, s>>>(static_cast<const uint4*>(staging), world, M, nl / 8,
                                                                static_cast<uint4*>(y), ldy / 8);

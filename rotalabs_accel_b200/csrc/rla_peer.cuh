@@ -31,8 +31,9 @@
 // The call number s is one more than the calls this rank has completed (a
 // counter in its sync area, advanced by the last unpacking CTA).  Every wait is
 // bounded by PeerOut::wait_ns; a wait that gives up records a device error and
-// marks the call aborted (the other waits of the call stop at once; y is then
-// incomplete).
+// marks the exchange aborted: the other waits of the call stop at once (y is
+// then incomplete), and so do those of every later call on the same sync area
+// (device error RLA_DEVERR_PEER_POISONED), until the exchange is set up again.
 #pragma once
 
 #include "rla_common.cuh"
@@ -45,14 +46,28 @@ RLA_DEVFN unsigned int rla_ld_relaxed_gpu_u32(const unsigned int* p) {
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// One flagged word {data, flag}: 8-byte aligned, written and read whole.
+// One flagged word {data (low 32 bits), flag (high 32 bits)}: one aligned
+// scalar 64-bit access each way.  A naturally aligned scalar access is
+// single-copy atomic in the PTX memory model, so a reader sees the flag and
+// the data of the same store.  (A vector access such as v2.u32 is two 32-bit
+// accesses in unspecified order, which would not give this guarantee.)
 RLA_DEVFN void rla_st_flagged(uint2* p, uint32_t data, uint32_t flag) {
-  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(flag) : "memory");
+  const uint64_t v = static_cast<uint64_t>(data) | (static_cast<uint64_t>(flag) << 32);
+  asm volatile("st.volatile.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 RLA_DEVFN uint2 rla_ld_flagged(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
+  uint64_t v;
+  asm volatile("ld.volatile.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return make_uint2(static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32));
+}
+// Two consecutive flagged words (16-byte aligned) in one load: two 64-bit
+// elements, each single-copy atomic on its own; each word carries its own
+// flag, so the pair needs no more than that.
+RLA_DEVFN void rla_ld_flagged2(const uint2* p, uint2& a, uint2& b) {
+  uint64_t u, v;
+  asm volatile("ld.volatile.global.v2.b64 {%0, %1}, [%2];" : "=l"(u), "=l"(v) : "l"(p) : "memory");
+  a = make_uint2(static_cast<uint32_t>(u), static_cast<uint32_t>(u >> 32));
+  b = make_uint2(static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32));
 }
 
 // This launch's call number.  Read after the dependency wait: the previous
@@ -88,7 +103,7 @@ RLA_DEVFN bool peer_wait_word(const PeerOut& po, const uint2* w, unsigned int s,
     __nanosleep(100);
     out = rla_ld_flagged(w);
     if (out.y == s) return true;
-    if (rla_ld_relaxed_gpu_u32(abort_word) == s) return false;  // another wait of this call gave up
+    if (rla_ld_relaxed_gpu_u32(abort_word) != 0u) return false;  // a wait of this call gave up
     if (rla_globaltimer() - t0 > po.wait_ns) {
       rla_record_error(RLA_DEVERR_TIMEOUT_PEER_DATA);
       atomicExch(po.sync + kSyncAbort, s);
@@ -97,9 +112,25 @@ RLA_DEVFN bool peer_wait_word(const PeerOut& po, const uint2* w, unsigned int s,
   }
 }
 
+// One received flagged word (pair p, column n of source rank src; pc = p *
+// n_local + n) into y.
+RLA_DEVFN void peer_unpack_word(uint2 v, __half* y, int64_t ldy, int M, int n_local, int src, int64_t pc) {
+  const int p = static_cast<int>(pc / n_local);
+  const int n = static_cast<int>(pc - (int64_t)p * n_local);
+  const int64_t col = (int64_t)src * n_local + n;
+  y[(int64_t)(2 * p) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x & 0xffffu));
+  if (2 * p + 1 < M) y[(int64_t)(2 * p + 1) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x >> 16));
+}
+
 // Phase 2.  Called by the `nthreads` threads of a CTA that take part in named
 // barrier `bar_id` (thread index tid), after their last phase-1 store; `slot`
 // is a shared-memory int of the CTA.
+//
+// An exchange whose wait once gave up stays failed: the abort word of the
+// sync area is never cleared, and every later call records
+// RLA_DEVERR_PEER_POISONED and skips its waits at once (y incomplete) instead
+// of waiting out its own limit.  The exchange must be closed and set up again
+// by every rank.
 RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t ldy, int M, int n_local, int tid,
                            int nthreads, int bar_id, int* slot) {
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
@@ -113,33 +144,66 @@ RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t
   const int u = *slot;
   if (u < 0) return;  // not an unpacker: this CTA is done
   const uint64_t t0 = rla_globaltimer();
+  const bool poisoned = rla_ld_relaxed_gpu_u32(po.sync + kSyncAbort) != 0u;  // an earlier call gave up
   if (tid == 0) {
-    // Wait until every CTA of the launch has finished phase 1.
-    while (rla_ld_relaxed_gpu_u32(po.sync + kSyncArrive) < ctas) {
-      if (rla_ld_relaxed_gpu_u32(po.sync + kSyncAbort) == s) break;
-      if (rla_globaltimer() - t0 > po.wait_ns) {
-        rla_record_error(RLA_DEVERR_TIMEOUT_GRID);
-        atomicExch(po.sync + kSyncAbort, s);
-        break;
+    if (poisoned) {
+      rla_record_error(RLA_DEVERR_PEER_POISONED);
+    } else {
+      // Wait until every CTA of the launch has finished phase 1.
+      while (rla_ld_relaxed_gpu_u32(po.sync + kSyncArrive) < ctas) {
+        if (rla_ld_relaxed_gpu_u32(po.sync + kSyncAbort) != 0u) break;
+        if (rla_globaltimer() - t0 > po.wait_ns) {
+          rla_record_error(RLA_DEVERR_TIMEOUT_GRID);
+          atomicExch(po.sync + kSyncAbort, s);
+          break;
+        }
+        __nanosleep(100);
       }
-      __nanosleep(100);
     }
   }
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
   const int pairs = (M + 1) / 2;
   const int64_t per_src = (int64_t)pairs * n_local;
   const int64_t total = per_src * (po.world - 1);
-  for (int64_t w = (int64_t)u * nthreads + tid; w < total; w += (int64_t)R * nthreads) {
-    const int si = static_cast<int>(w / per_src);
-    const int src = si < po.rank ? si : si + 1;
-    const int64_t pc = w - (int64_t)si * per_src;
-    uint2 v;
-    if (!peer_wait_word(po, peer_word(po, po.rank, s, src, pc), s, v, t0)) break;
-    const int p = static_cast<int>(pc / n_local);
-    const int n = static_cast<int>(pc - (int64_t)p * n_local);
-    const int64_t col = (int64_t)src * n_local + n;
-    y[(int64_t)(2 * p) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x & 0xffffu));
-    if (2 * p + 1 < M) y[(int64_t)(2 * p + 1) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x >> 16));
+  // Units of two words (one 16-byte load) when every source slot starts on a
+  // 16-byte boundary, else single words.  Each thread issues kBatch unit
+  // loads before it looks at any flag; a word whose flag is not yet s is then
+  // waited for on its own.
+  const int wpu = (po.half_words % 2 == 0 && per_src % 2 == 0) ? 2 : 1;
+  const int64_t units = total / wpu;
+  const int64_t stride = (int64_t)R * nthreads;
+  constexpr int kBatch = 4;
+  bool live = !poisoned;
+  for (int64_t base = (int64_t)u * nthreads + tid; live && base < units; base += kBatch * stride) {
+    uint2 v[kBatch][2];
+    int src[kBatch];
+    int64_t pc[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int64_t unit = base + b * stride;
+      src[b] = -1;
+      if (unit < units) {
+        const int64_t w = unit * wpu;
+        const int si = static_cast<int>(w / per_src);
+        src[b] = si < po.rank ? si : si + 1;
+        pc[b] = w - (int64_t)si * per_src;
+        const uint2* a = peer_word(po, po.rank, s, src[b], pc[b]);
+        if (wpu == 2) rla_ld_flagged2(a, v[b][0], v[b][1]);
+        else v[b][0] = rla_ld_flagged(a);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      if (src[b] < 0 || !live) continue;
+      for (int j = 0; j < wpu; ++j) {
+        uint2 word = v[b][j];
+        if (word.y != s && !peer_wait_word(po, peer_word(po, po.rank, s, src[b], pc[b] + j), s, word, t0)) {
+          live = false;
+          break;
+        }
+        peer_unpack_word(word, y, ldy, M, n_local, src[b], pc[b] + j);
+      }
+    }
   }
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
   if (tid == 0) {

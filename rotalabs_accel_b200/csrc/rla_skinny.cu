@@ -34,6 +34,8 @@
 // With a peer exchange (PEER, rla_w8a16_gemm_allgather) the epilogue stores
 // pairs of rows into y and, as flagged words, into every peer's receive
 // buffer, and every CTA ends with peer_finish (rla_peer.cuh).
+#include <atomic>
+
 #include "rla_common.cuh"
 #include "rla_internal.h"
 #include "rla_peer.cuh"
@@ -44,6 +46,25 @@ template <int NT>
 struct XFrag {
   uint4 v[NT][2];
 };
+
+// One 64-wide k chunk of a warp: rows g and g+8 (wa[0], wa[1]: 16 int8 each)
+// times the chunk's activation fragments, four m16n8k16 steps per 8-token tile.
+template <int NT>
+RLA_DEVFN void skinny_chunk_mma(float (&acc)[NT][4], const uint4 (&wa)[2], const XFrag<NT>& xb) {
+  const uint32_t* w0 = reinterpret_cast<const uint32_t*>(&wa[0]);
+  const uint32_t* w1 = reinterpret_cast<const uint32_t*>(&wa[1]);
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    uint32_t a0, a1, a2, a3;
+    rla_i8x4_to_h2x2(w0[s], a0, a2);  // row g:   k {2q,2q+1} and {2q+8,2q+9}
+    rla_i8x4_to_h2x2(w1[s], a1, a3);  // row g+8
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xb.v[t][0]);
+      rla_mma_16816(acc[t], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
+    }
+  }
+}
 
 template <int NT, int WN, int WK, int U, bool PEER, bool GLU, bool XJ>
 __global__ void __launch_bounds__(32 * WN * WK)
@@ -113,6 +134,18 @@ __global__ void __launch_bounds__(32 * WN * WK)
   if constexpr (PEER) call = peer_call(po);
   __shared__ int peer_slot;
 
+  // The epilogue's scales and biases (already warmed in L2 above) are pulled
+  // into this SM's L1 now, so that the epilogue's loads hit L1 instead of
+  // adding an L2 round trip after the weight stream.
+  if (wk == 0 && q == 0) {
+    const int esz = scale_f32 ? 4 : 2, bsz = bias_kind == 2 ? 4 : 2;
+    rla_prefetch_l1(static_cast<const char*>(scale) + (int64_t)r0 * esz);
+    rla_prefetch_l1(static_cast<const char*>(GLU ? scale_up : scale) + (int64_t)r1 * esz);
+    if (bias_kind != 0) {
+      rla_prefetch_l1(static_cast<const char*>(bias) + (int64_t)r0 * bsz);
+      rla_prefetch_l1(static_cast<const char*>(GLU ? bias_up : bias) + (int64_t)r1 * bsz);
+    }
+  }
 
   const uint4 zero4 = make_uint4(0, 0, 0, 0);
   // XJIT: each chunk's activation fragments are loaded just before its MMAs
@@ -154,19 +187,7 @@ __global__ void __launch_bounds__(32 * WN * WK)
           xb[u].v[t][1] = okx ? rla_ldg_keep(xrow[t] + kofs + 8) : zero4;
         }
       }
-      const uint32_t* w0 = reinterpret_cast<const uint32_t*>(&wa[u][0]);
-      const uint32_t* w1 = reinterpret_cast<const uint32_t*>(&wa[u][1]);
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        uint32_t a0, a1, a2, a3;
-        rla_i8x4_to_h2x2(w0[s], a0, a2);  // row g:   k {2q,2q+1} and {2q+8,2q+9}
-        rla_i8x4_to_h2x2(w1[s], a1, a3);  // row g+8
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xb[u].v[t][0]);
-          rla_mma_16816(acc[t], a0, a1, a2, a3, xw[2 * s], xw[2 * s + 1]);
-        }
-      }
+      skinny_chunk_mma<NT>(acc, wa[u], xb[u]);
     }
   }
 
@@ -371,8 +392,79 @@ __global__ void __launch_bounds__(32 * WN * WK)
   if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
 }
 
-template <int NT, int WN, int WK, int U, bool XJ>
+// ---------------------------------------------------------------------------
+// Host side.  Per-device facts about an instantiation (its dynamic
+// shared-memory attribute, its occupancy) are cached per device, lock-free:
+// a race only repeats a query.
+// ---------------------------------------------------------------------------
+constexpr int kSkMaxDevices = 64;
+
+static int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kSkMaxDevices) return -1;
+  return d;
+}
+
+// The kernel instance of a configuration and form (0 plain, 1 gated, 2 with
+// the peer exchange).
+template <int NT, int WN, int WK, bool XJ>
+struct SkinnyInst {
+  static constexpr int U = NT >= 4 ? 2 : 4;
+  static constexpr int THREADS = 32 * WN * WK;
+  static constexpr size_t SMEM = 0;
+  using KernT = void (*)(const __half*, int64_t, const int8_t*, int64_t, const void*, int, const void*, int,
+                         __half*, int64_t, int, int, int, int, float*, unsigned int*, const PeerOut, const int8_t*,
+                         const void*, const void*);
+  static KernT kernel(int form) {
+    return form == 1   ? w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>
+           : form == 2 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>
+                       : w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>;
+  }
+  // CTAs that can be resident on the whole device at once when the K slices
+  // of a row block form clusters of `cluster` CTAs (1: no cluster).  With
+  // clusters this counts whole clusters that fit (all CTAs of a cluster sit
+  // in one GPC), not just CTAs per SM.  0 when the device cannot be asked.
+  static int resident(int form, int cluster) {
+    static std::atomic<int> cache[kSkMaxDevices][3][kMaxClusterSplits + 1];
+    const int d = current_device();
+    if (d < 0 || cluster < 1 || cluster > kMaxClusterSplits) return 0;
+    const int cached = cache[d][form][cluster].load(std::memory_order_relaxed);
+    if (cached > 0) return cached;
+    int v = 0;
+    cudaError_t e;
+    if (cluster == 1) {
+      int per_sm = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel(form), THREADS, SMEM);
+      v = per_sm * device_sm_count();
+    } else {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, cluster);
+      cfg.blockDim = dim3(THREADS);
+      cfg.dynamicSmemBytes = SMEM;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = static_cast<unsigned int>(cluster);
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&clusters, kernel(form), &cfg);
+      v = clusters * cluster;
+    }
+    if (e != cudaSuccess || v < 1) {
+      (void)cudaGetLastError();
+      return 0;
+    }
+    cache[d][form][cluster].store(v, std::memory_order_relaxed);
+    return v;
+  }
+};
+
+template <int NT, int WN, int WK, bool XJ>
 static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s) {
+  using I = SkinnyInst<NT, WN, WK, XJ>;
+  const int form = a.w_up ? 1 : a.peer.world > 0 ? 2 : 0;
   const int total_chunks = (a.K + 63) / 64;
   const int cps = (total_chunks + p.splits - 1) / p.splits;
   unsigned int* counters = nullptr;
@@ -383,43 +475,37 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid_x, p.splits);
-  cfg.blockDim = dim3(32 * WN * WK);
-  cfg.dynamicSmemBytes = 0;
+  cfg.blockDim = dim3(I::THREADS);
+  cfg.dynamicSmemBytes = I::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see rla_griddep_wait
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (p.splits > 1 && p.cluster) {
+  const int cluster = p.splits > 1 && p.cluster ? p.splits : 1;
+  if (cluster > 1) {
     // the K slices of a row block are one cluster (split-K through
     // distributed shared memory)
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = static_cast<unsigned int>(p.splits);
+    attr[1].val.clusterDim.y = static_cast<unsigned int>(cluster);
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
   }
-  auto kern = a.w_up ? w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>
-              : a.peer.world > 0 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>
-                                 : w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>;
   PeerOut po = a.peer;
   if (po.world > 0) {
-    // Unpacking CTAs: the whole grid when it is resident at once, else at
-    // most (resident + 1) / 2 so that the CTAs still to run find room.
-    static int per_sm = -1;
-    if (per_sm < 0) {
-      int v = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, 32 * WN * WK, 0) != cudaSuccess || v < 1) v = 1;
-      per_sm = v;
-    }
+    // Unpacking CTAs: the whole grid when it is resident at once (counted in
+    // whole clusters), else at most (resident + 1) / 2 so that the CTAs still
+    // to run find room.
+    int resident = I::resident(form, cluster);
+    if (resident < 1) resident = 1;
     const unsigned int ctas = static_cast<unsigned int>(p.grid_x) * static_cast<unsigned int>(p.splits);
-    const unsigned int resident = static_cast<unsigned int>(per_sm * device_sm_count());
-    po.unpackers = ctas <= resident ? ctas : (resident + 1) / 2;
+    po.unpackers = ctas <= (unsigned)resident ? ctas : ((unsigned)resident + 1) / 2;
   }
-  return cudaLaunchKernelEx(&cfg, kern, static_cast<const __half*>(a.x), a.ldx, a.w,
-                            a.ldw, a.scale, a.scale_f32, a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M,
-                            a.N, a.K, cps, partial, counters, po, a.w_up, a.scale_up, a.bias_up);
+  return cudaLaunchKernelEx(&cfg, I::kernel(form), static_cast<const __half*>(a.x), a.ldx, a.w, a.ldw, a.scale,
+                            a.scale_f32, a.bias, a.bias_kind, static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K, cps,
+                            partial, counters, po, a.w_up, a.scale_up, a.bias_up);
 }
 
 // Instantiated configurations: NT in {1, 2, 4}; (WN, WK) in {(1, 8), (2, 4),
@@ -427,66 +513,47 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
 // NT = 1 with (1, 8); for NT = 2 with (1, 4) when the plan asks for it.
 template <int NT>
 static cudaError_t launch_nt(const GemmArgs& a, const Plan& p, void* ws, cudaStream_t s) {
-  constexpr int U = NT >= 4 ? 2 : 4;
-  if (p.wn == 1 && p.wk == 8) return launch_cfg<NT, 1, 8, U, NT == 1>(a, p, ws, s);
-  if (p.wn == 2 && p.wk == 4) return launch_cfg<NT, 2, 4, U, false>(a, p, ws, s);
-  if (p.wn == 4 && p.wk == 2) return launch_cfg<NT, 4, 2, U, false>(a, p, ws, s);
+  if (p.wn == 1 && p.wk == 8) return launch_cfg<NT, 1, 8, NT == 1>(a, p, ws, s);
+  if (p.wn == 2 && p.wk == 4) return launch_cfg<NT, 2, 4, false>(a, p, ws, s);
+  if (p.wn == 4 && p.wk == 2) return launch_cfg<NT, 4, 2, false>(a, p, ws, s);
   if (p.wn == 1 && p.wk == 4) {
     if constexpr (NT == 2) {
-      if (p.xjit) return launch_cfg<NT, 1, 4, U, true>(a, p, ws, s);
+      if (p.xjit) return launch_cfg<NT, 1, 4, true>(a, p, ws, s);
     }
-    return launch_cfg<NT, 1, 4, U, false>(a, p, ws, s);
+    return launch_cfg<NT, 1, 4, false>(a, p, ws, s);
   }
   return cudaErrorInvalidConfiguration;
 }
 
-// Resident CTAs per SM of one instantiation: form 0 plain, 1 gated (GLU),
-// 2 with the peer exchange (PEER).  Queried once per form and cached.
-template <int NT, int WN, int WK, bool XJ>
-static int ctas_per_sm_cfg(int form) {
-  constexpr int U = NT >= 4 ? 2 : 4;
-  static int cache[3] = {-1, -1, -1};
-  int& c = cache[form];
-  if (c < 0) {
-    int v = 0;
-    const cudaError_t e =
-        form == 1   ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                        &v, w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>, 32 * WN * WK, 0)
-        : form == 2 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                          &v, w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>, 32 * WN * WK, 0)
-                    : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                          &v, w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>, 32 * WN * WK, 0);
-    if (e != cudaSuccess || v < 1) {
-      (void)cudaGetLastError();
-      return 2;   // no device to ask (e.g. planning on a CPU-only host)
-    }
-    c = v;
-  }
-  return c;
-}
-
 template <int NT>
-static int ctas_per_sm_nt(int wn, int wk, int form, bool xjit) {
-  if (wn == 1 && wk == 8) return ctas_per_sm_cfg<NT, 1, 8, NT == 1>(form);
-  if (wn == 2 && wk == 4) return ctas_per_sm_cfg<NT, 2, 4, false>(form);
-  if (wn == 4 && wk == 2) return ctas_per_sm_cfg<NT, 4, 2, false>(form);
+static int resident_nt(int wn, int wk, int form, bool xjit, int cluster) {
+  if (wn == 1 && wk == 8) return SkinnyInst<NT, 1, 8, NT == 1>::resident(form, cluster);
+  if (wn == 2 && wk == 4) return SkinnyInst<NT, 2, 4, false>::resident(form, cluster);
+  if (wn == 4 && wk == 2) return SkinnyInst<NT, 4, 2, false>::resident(form, cluster);
   if (wn == 1 && wk == 4) {
     if constexpr (NT == 2) {
-      if (xjit) return ctas_per_sm_cfg<NT, 1, 4, true>(form);
+      if (xjit) return SkinnyInst<NT, 1, 4, true>::resident(form, cluster);
     }
-    return ctas_per_sm_cfg<NT, 1, 4, false>(form);
+    return SkinnyInst<NT, 1, 4, false>::resident(form, cluster);
   }
-  return 2;
+  return 0;
+}
+
+int skinny_resident_ctas(int nt, int wn, int wk, bool gated, bool xjit, bool peer, int cluster) {
+  const int form = gated ? 1 : peer ? 2 : 0;
+  int v = 0;
+  switch (nt) {
+    case 1: v = resident_nt<1>(wn, wk, form, xjit, cluster); break;
+    case 2: v = resident_nt<2>(wn, wk, form, xjit, cluster); break;
+    case 4: v = resident_nt<4>(wn, wk, form, xjit, cluster); break;
+    default: break;
+  }
+  // no device to ask (e.g. planning on a CPU-only host): two CTAs per SM
+  return v > 0 ? v : 2 * device_sm_count();
 }
 
 int skinny_ctas_per_sm(int nt, int wn, int wk, bool gated, bool xjit, bool peer) {
-  const int form = gated ? 1 : peer ? 2 : 0;
-  switch (nt) {
-    case 1: return ctas_per_sm_nt<1>(wn, wk, form, xjit);
-    case 2: return ctas_per_sm_nt<2>(wn, wk, form, xjit);
-    case 4: return ctas_per_sm_nt<4>(wn, wk, form, xjit);
-    default: return 2;
-  }
+  return skinny_resident_ctas(nt, wn, wk, gated, xjit, peer, 1) / device_sm_count();
 }
 
 cudaError_t launch_skinny(const GemmArgs& a, const Plan& p, void* workspace, cudaStream_t s) {

@@ -254,6 +254,7 @@ static cudaError_t launch_tc_cfg(const GemmArgs& a, const Plan& p, cudaStream_t 
   cudaError_t attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (attr_err != cudaSuccess) return attr_err;
   dim3 grid(p.grid_x, p.grid_y);
+  rla_clear_stale_launch_error();
   kern<<<grid, tc::THREADS, smem, s>>>(tx, tw, a.scale, a.scale_f32, a.bias, a.bias_kind,
                                         static_cast<__half*>(a.y), a.ldy, a.M, a.N, a.K);
   return cudaGetLastError();

@@ -18,6 +18,13 @@ over the process group, maps every peer's buffer, and keeps a local sync
 area.  ``exchange.gemm(x2d, weight_int8, scale, bias)`` then runs on every
 rank, in the same order and with the same shapes on every rank,
 stream-ordered on each rank.  ``close()`` (collective) unmaps and frees.
+
+Failure: every wait inside an exchange call is bounded.  A wait that gives up
+(a peer that never sends its slice) marks this rank's sync area, and from then
+on every exchange call on it returns at once with its output incomplete
+(device errors 7, 8 and then 9).  ``check()`` reads the mark; once it is
+seen, ``gemm`` refuses further calls.  Recovery is collective: ``close()`` on
+every rank, then a new ``PeerExchange``.
 """
 
 from __future__ import annotations
@@ -123,10 +130,22 @@ class PeerExchange:
         header = struct.pack("<qqq", self.world, max_rows, max_n_local)
         self._recv = _SharedBuffer(self.recv_bytes, group, self.rank, header)
         self._sync = torch.zeros(_capi.PEER_SYNC_BYTES // 4, dtype=torch.int32, device=self.device)
+        self._failed: Optional[str] = None
 
     def calls_completed(self) -> int:
         """Exchange calls this rank has completed (synchronises)."""
         return int(self._sync[0].item())
+
+    def check(self) -> None:
+        """Raise if a wait of an exchange call on this rank gave up
+        (synchronises with the device).  From then on ``gemm`` refuses
+        further calls: ``close()`` this exchange on every rank and create a
+        new one."""
+        if self._failed is None and int(self._sync[_capi.PEER_SYNC_ABORT_WORD].item()) != 0:
+            self._failed = (f"a wait of exchange call {int(self._sync[_capi.PEER_SYNC_ABORT_WORD].item())} gave up "
+                            "(a peer's slice or this launch's CTAs did not arrive in time)")
+        if self._failed is not None:
+            raise RuntimeError(f"PeerExchange failed: {self._failed}; close() it on every rank and set up a new one")
 
     def gemm(self, x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
              bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -135,6 +154,8 @@ class PeerExchange:
         here from its shard ``weight_int8 [n_local, K]``."""
         if self._recv is None:
             raise RuntimeError("PeerExchange is closed")
+        if self._failed is not None:
+            raise RuntimeError(f"PeerExchange failed: {self._failed}; close() it on every rank and set up a new one")
         M = x2d.shape[0]
         n_local = weight_int8.shape[0]
         if M > self.max_rows or n_local > self.max_n_local:

@@ -71,10 +71,10 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
 
 
 def test_selector_rules(lib):
-    # decode regime: the persistent stream-K kernel on large weights (and from
-    # M = 9 on weights >= 40 MB whose skinny grid is more than one wave), the
-    # skinny kernel otherwise.  Without a device the occupancy query falls back
-    # to 2 resident CTAs per SM on 148 SMs.
+    # decode regime: from M = 9 on, the persistent stream-K kernel on large
+    # weights (>= 120 MB, or >= 40 MB when the skinny grid is more than one
+    # wave); the skinny kernel otherwise (M <= 8 always).  Without a device the
+    # occupancy query falls back to 2 resident CTAs per SM on 148 SMs.
     for M in (1, 4, 8, 16, 32):
         for K, N in ((4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336), (8192, 28672), (28672, 1024)):
             _capi.set_decode_kernel("skinny")
@@ -84,7 +84,7 @@ def test_selector_rules(lib):
                 _capi.set_decode_kernel("auto")
             multi_wave = sk["grid_x"] > 2 * 148
             p = _capi.plan(M, N, K)
-            big = M <= 16 and ((M > 8 and N * K >= 40e6 and multi_wave) or N * K >= 120e6)
+            big = 8 < M <= 16 and ((N * K >= 40e6 and multi_wave) or N * K >= 120e6)
             assert (M, K, N, p["kernel_name"]) != (16, 11008, 4096, "stream")
             assert p["kernel_name"] == ("stream" if big else "skinny"), (M, N, K)
             assert p["x_rows"] >= M and p["x_rows"] <= 32

@@ -142,3 +142,29 @@ def test_layer_refuses_peer_exchange_on_cpu():
         m.enable_peer_exchange(max_tokens=4)
     with pytest.raises(ValueError):
         m.enable_peer_exchange(max_tokens=64)
+
+
+def test_exchange_refuses_calls_after_a_failed_wait():
+    """Once a wait of an exchange call has given up (the abort word of the
+    sync area is set), check() raises and gemm() refuses every later call
+    until the exchange is set up again.  Host logic only: the exchange object
+    is assembled by hand around a CPU sync area."""
+    from rotalabs_accel_b200 import _capi
+    from rotalabs_accel_b200.peer import PeerExchange
+    ex = PeerExchange.__new__(PeerExchange)
+    ex._recv = object()                    # "open"
+    ex._failed = None
+    ex.max_rows, ex.max_n_local = 16, 128
+    ex._sync = torch.zeros(_capi.PEER_SYNC_BYTES // 4, dtype=torch.int32)
+    ex.check()                             # a clean sync area passes
+    ex._sync[_capi.PEER_SYNC_ABORT_WORD] = 5
+    with pytest.raises(RuntimeError, match="call 5 gave up"):
+        ex.check()
+    x = torch.zeros(1, 64, dtype=torch.float16)
+    w = torch.zeros(128, 64, dtype=torch.int8)
+    s = torch.ones(128, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="set up a new one"):
+        ex.gemm(x, w, s)
+    ex._sync[_capi.PEER_SYNC_ABORT_WORD] = 0  # the mark stays on the host side too
+    with pytest.raises(RuntimeError, match="PeerExchange failed"):
+        ex.check()
