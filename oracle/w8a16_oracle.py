@@ -131,35 +131,6 @@ def int8_gemm(x, weight_int8, scale, bias=None, weight_transposed=None, scale_fp
     return int8_gemm_torch(x, weight_int8, scale, bias)
 
 
-def int8_gemm_parallel(x, weight_int8, scale, bias=None, threads: int = 1):
-    """``int8_gemm_torch`` with the output channels split over a thread pool
-    (numpy releases the GIL in its array kernels): the same per-row
-    arithmetic, so each output element equals the serial result's up to
-    BLAS summation order.  Used to time the reference algorithm on all host
-    cores."""
-    from concurrent.futures import ThreadPoolExecutor
-    x = np.asarray(x)
-    N, K = weight_int8.shape
-    threads = max(1, int(threads))
-    if threads == 1 or N < 2 * threads:
-        return int8_gemm_torch(x, weight_int8, scale, bias)
-    x2 = x.reshape(-1, K).astype(np.float32)
-    out = np.empty((x2.shape[0], N), dtype=x.dtype)
-    bounds = np.linspace(0, N, threads + 1).astype(int)
-
-    def part(i):
-        lo, hi = bounds[i], bounds[i + 1]
-        w_deq = dequantize(weight_int8[lo:hi], scale[lo:hi], dtype=x.dtype, dim=0)
-        acc = x2 @ w_deq.astype(np.float32).T
-        if bias is not None:
-            acc = acc + np.asarray(bias[lo:hi]).astype(np.float32)
-        out[:, lo:hi] = acc.astype(x.dtype)
-
-    with ThreadPoolExecutor(threads) as ex:
-        list(ex.map(part, range(threads)))
-    return out.reshape(x.shape[:-1] + (N,))
-
-
 def dequant_matmul_fp32(x, weight_int8, scale, bias=None):
     """The tolerance reference of the north star: fp32-accumulated
     dequant-matmul, ``x.float() @ (w.float() * s.float()[:, None]).T (+ bias)``,

@@ -10,6 +10,9 @@ The per-token hot calls (``w8a16_gemm``, ``w8a16_gemm_swiglu``) go through
 ``_rla_fast``, CPython fast-call bindings of the same entry points linked to
 the same library (ctypes' generic argument conversion costs more host time
 than a decode GEMM takes on the GPU).  Without that module they use ctypes.
+A call without a preallocated output goes through ``torch.ops.rla.w8a16_gemm``
+(``_rla_torch_ops.so``, a C++ ``torch.library`` registration over the same C
+ABI that allocates the output with torch's allocator), when it loads.
 """
 
 from __future__ import annotations
@@ -22,6 +25,7 @@ import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "librla_w8a16.so")
+TORCH_OP_PATH = os.path.join(_HERE, "_rla_torch_ops.so")
 
 RLA_OK = 0
 DTYPE_NONE, DTYPE_F16, DTYPE_F32, DTYPE_BF16 = 0, 1, 2, 3
@@ -44,6 +48,7 @@ IPC_HANDLE_BYTES = 64
 
 _lib = None
 _fast = None
+_torch_op = None
 _lib_lock = threading.Lock()
 
 
@@ -119,6 +124,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                 globals()["_fast"] = _rla_fast
             except ImportError:
                 pass
+            if os.path.exists(TORCH_OP_PATH):
+                try:
+                    torch.ops.load_library(TORCH_OP_PATH)
+                    globals()["_torch_op"] = torch.ops.rla.w8a16_gemm.default
+                except (OSError, RuntimeError):
+                    pass
         _lib = lib
         return lib
 
@@ -181,6 +192,8 @@ def w8a16_gemm(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor
     ``[N, K]`` with unit inner stride; ``scale`` ``[N]`` fp32/fp16
     contiguous; ``bias`` ``[N]`` fp16/fp32 or None."""
     lib = _lib if _lib is not None else load_library()
+    if out is None and _torch_op is not None:
+        return _torch_op(x2d, weight_int8, scale, bias)
     fast = _fast
     M, K = x2d.shape
     N = weight_int8.shape[0]
@@ -365,6 +378,12 @@ def ipc_open(handle: bytes) -> int:
 
 def ipc_close(ptr: int) -> None:
     _check(load_library().rla_ipc_close(ptr), "rla_ipc_close")
+
+
+def torch_op_loaded() -> bool:
+    """Whether ``torch.ops.rla.w8a16_gemm`` is registered (``_rla_torch_ops.so``)."""
+    load_library()
+    return _torch_op is not None
 
 
 def launch_count() -> int:

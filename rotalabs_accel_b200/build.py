@@ -10,7 +10,11 @@ statically; the driver's tensor-map encoder is reached through
 
 Then compiles ``csrc/rla_pyfast.c``, the CPython fast-call bindings of the
 hot entry points, with the host C compiler into ``_rla_fast<EXT_SUFFIX>``
-next to the library, linked to it by soname with an ``$ORIGIN`` rpath.
+next to the library, linked to it by soname with an ``$ORIGIN`` rpath; and
+``csrc/rla_torch_op.cpp``, the ``torch.library`` registration of
+``rla::w8a16_gemm`` over the same C ABI, against the installed torch's
+headers and libraries into ``_rla_torch_ops.so`` (loaded with
+``torch.ops.load_library``).
 """
 
 from __future__ import annotations
@@ -26,6 +30,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "librla_w8a16.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 FAST_PATH = os.path.join(HERE, "_rla_fast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+TORCH_OP_PATH = os.path.join(HERE, "_rla_torch_ops.so")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -58,10 +63,38 @@ def _sources():
 
 
 def needs_build() -> bool:
-    if not os.path.exists(LIB_PATH) or not os.path.exists(FAST_PATH):
+    outs = (LIB_PATH, FAST_PATH, TORCH_OP_PATH)
+    if not all(os.path.exists(o) for o in outs):
         return True
-    t = min(os.path.getmtime(LIB_PATH), os.path.getmtime(FAST_PATH))
-    return any(os.path.getmtime(s) > t for s in _sources() + [os.path.join(CSRC, "rla_pyfast.c")])
+    t = min(os.path.getmtime(o) for o in outs)
+    extra = [os.path.join(CSRC, "rla_pyfast.c"), os.path.join(CSRC, "rla_torch_op.cpp")]
+    return any(os.path.getmtime(s) > t for s in _sources() + extra)
+
+
+def build_torch_op(verbose: bool = False) -> str:
+    """Compile the torch.library registration (rla::w8a16_gemm) against the
+    installed torch and the built library."""
+    import torch
+    from torch.utils import cpp_extension
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if not cxx:
+        raise RuntimeError("no host C++ compiler found for the torch op registration")
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(_nvcc())), "include")
+    tlib = cpp_extension.library_paths()[0]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = TORCH_OP_PATH + ".tmp"
+    cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           *[f"-I{p}" for p in cpp_extension.include_paths()], f"-I{cuda_inc}",
+           os.path.join(CSRC, "rla_torch_op.cpp"), "-L" + HERE, "-l:" + LIB_NAME, f"-L{tlib}",
+           "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tlib}", "-o", tmp]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"building the torch op registration failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, TORCH_OP_PATH)
+    return TORCH_OP_PATH
 
 
 def build_fast(verbose: bool = False) -> str:
@@ -93,6 +126,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
         print(r.stdout, r.stderr, file=sys.stderr)
     os.replace(tmp, LIB_PATH)
     build_fast(verbose)
+    build_torch_op(verbose)
     return LIB_PATH
 
 

@@ -96,11 +96,20 @@ def int8_gemm(x: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
 class Int8Linear(torch.nn.Module):
     """Linear layer with int8 weights and per-output-channel scales.
 
-    Buffers (the reference's state-dict layout, kept byte-compatible):
-    ``weight_int8`` int8 ``[out, in]``, ``scale`` fp32 ``[out]``,
-    ``weight_transposed`` int8 ``[in, out]`` and an optional fp16 ``bias``
-    Parameter.  ``weight_transposed`` is filled for compatibility with
-    checkpoints and code that read it; the sm_100a kernels do not use it.
+    State dict (the reference's layout, byte-compatible,
+    src/rotalabs_accel/kernels/gemm.py:266-286): ``weight_int8`` int8
+    ``[out, in]``, ``scale`` fp32 ``[out]``, ``weight_transposed`` int8
+    ``[in, out]`` and an optional fp16 ``bias`` Parameter, in that order
+    after the bias.
+
+    Only ``weight_int8`` and ``scale`` (and ``bias``) live on the device.  The
+    reference keeps a second, transposed copy of every weight for its Triton
+    path (gemm.py:276-281, :302); the sm_100a kernels read ``weight_int8``
+    directly, so here ``weight_transposed`` is a transposed *view* of
+    ``weight_int8`` (no extra memory), materialized as a contiguous ``[in,
+    out]`` tensor only when the state dict is saved, and checked against
+    ``weight_int8`` (not stored) when one is loaded.
+
     ``_quantized`` is a plain attribute, not saved: a module restored with
     ``load_state_dict`` must be re-marked (``quantize_weights`` or
     ``mark_quantized()``) before ``forward``, as in the reference.
@@ -112,12 +121,39 @@ class Int8Linear(torch.nn.Module):
         self.out_features = out_features
         self.register_buffer("weight_int8", torch.zeros(out_features, in_features, dtype=torch.int8))
         self.register_buffer("scale", torch.ones(out_features, dtype=torch.float32))
-        self.register_buffer("weight_transposed", torch.zeros(in_features, out_features, dtype=torch.int8))
         if bias:
             self.bias = torch.nn.Parameter(torch.zeros(out_features, dtype=torch.float16))
         else:
             self.register_parameter("bias", None)
         self._quantized = False
+
+    @property
+    def weight_transposed(self) -> torch.Tensor:
+        """``weight_int8`` as ``[in, out]``: a view, not a copy."""
+        return self.weight_int8.t()
+
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        super()._save_to_state_dict(destination, prefix, keep_vars)
+        wt = self.weight_int8.t().contiguous()
+        destination[prefix + "weight_transposed"] = wt if keep_vars else wt.detach()
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        key = prefix + "weight_transposed"
+        wt = state_dict.get(key)
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
+        if key in unexpected_keys:
+            unexpected_keys.remove(key)
+        if wt is None:
+            if strict:
+                missing_keys.append(key)
+        elif tuple(wt.shape) != (self.in_features, self.out_features) or wt.dtype != torch.int8:
+            error_msgs.append(f"size mismatch for {key}: copying a param with shape {tuple(wt.shape)} "
+                              f"({wt.dtype}), expected ({self.in_features}, {self.out_features}) int8")
+        elif prefix + "weight_int8" in state_dict and not torch.equal(
+                wt.to(state_dict[prefix + "weight_int8"].device).t(), state_dict[prefix + "weight_int8"]):
+            error_msgs.append(f"{key} is not the transpose of {prefix}weight_int8")
 
     def quantize_weights(self, weight: torch.Tensor) -> None:
         """Quantize an ``[out, in]`` float weight into the int8 buffers.
@@ -130,7 +166,6 @@ class Int8Linear(torch.nn.Module):
         device = self.weight_int8.device
         self.weight_int8.copy_(q.to(device))
         self.scale.copy_(s.to(device))
-        self.weight_transposed.copy_(q.t().contiguous().to(device))
         self._quantized = True
 
     def mark_quantized(self) -> None:
@@ -140,7 +175,10 @@ class Int8Linear(torch.nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not self._quantized:
             raise RuntimeError("Weights not quantized. Call quantize_weights() first.")
-        return int8_gemm(x, self.weight_int8, self.scale, self.bias, weight_transposed=self.weight_transposed)
+        # (the buffer and parameter dicts directly: nn.Module attribute lookup
+        # costs host time on every decode call)
+        b = self._buffers
+        return int8_gemm(x, b["weight_int8"], b["scale"], self._parameters["bias"])
 
     @classmethod
     def from_linear(cls, linear: torch.nn.Linear) -> "Int8Linear":

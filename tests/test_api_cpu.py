@@ -132,6 +132,22 @@ def test_state_dict_layout():
     sd = ql.state_dict()
     assert list(sd) == ["bias", "weight_int8", "weight_scale"]
     assert sd["bias"].dtype == torch.float32
+    # weight_transposed is the reference's key, materialized on save from
+    # weight_int8 (no second copy is held by the module)
+    assert dict(il.named_buffers()).keys() == {"weight_int8", "scale"}
+    il.quantize_weights(torch.randn(128, 64))
+    assert torch.equal(il.state_dict()["weight_transposed"], il.weight_int8.t())
+    assert il.state_dict()["weight_transposed"].is_contiguous()
+    assert torch.equal(il.weight_transposed, il.weight_int8.t())
+    # a state dict whose weight_transposed disagrees with weight_int8 is refused
+    bad = il.state_dict()
+    bad["weight_transposed"] = bad["weight_transposed"].clone()
+    bad["weight_transposed"][0, 0] += 1
+    with pytest.raises(RuntimeError, match="transpose"):
+        ra.Int8Linear(64, 128, bias=True).load_state_dict(bad)
+    with pytest.raises(RuntimeError, match="weight_transposed"):
+        ra.Int8Linear(64, 128, bias=True).load_state_dict(
+            {k: v for k, v in il.state_dict().items() if k != "weight_transposed"})
     # _quantized is not persisted: a restored module must be re-marked
     il2 = ra.Int8Linear(64, 128, bias=True)
     il.quantize_weights(torch.randn(128, 64))

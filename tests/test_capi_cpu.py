@@ -181,3 +181,26 @@ def test_allgather_workspace_size():
     assert need > 4096 and need % 4 == 0
     assert lib.rla_w8a16_allgather_workspace_size(0, 14336, 8192) == 0
     assert lib.rla_w8a16_allgather_workspace_size(-1, 14336, 8192) == 0
+
+
+def test_torch_library_op_registered():
+    """rla::w8a16_gemm is registered with torch (CUDA and Meta kernels over
+    the C ABI); its Meta kernel gives shapes and the reference's checks
+    without a device."""
+    import torch
+    from rotalabs_accel_b200 import _capi
+    assert _capi.torch_op_loaded()
+    meta = dict(device="meta")
+    x = torch.empty(5, 96, dtype=torch.float16, **meta)
+    w = torch.empty(40, 96, dtype=torch.int8, **meta)
+    s = torch.empty(40, dtype=torch.float32, **meta)
+    y = torch.ops.rla.w8a16_gemm(x, w, s)
+    assert y.shape == (5, 40) and y.dtype == torch.float16 and y.device.type == "meta"
+    y = torch.ops.rla.w8a16_gemm(x, w, s.half(), torch.empty(40, dtype=torch.float16, **meta))
+    assert y.shape == (5, 40)
+    with pytest.raises(RuntimeError, match="Weight must be INT8"):
+        torch.ops.rla.w8a16_gemm(x, w.to(torch.float16), s)
+    with pytest.raises(RuntimeError, match="Scale shape mismatch"):
+        torch.ops.rla.w8a16_gemm(x, w, torch.empty(39, **meta))
+    with pytest.raises(RuntimeError, match="Weight shape mismatch"):
+        torch.ops.rla.w8a16_gemm(x, torch.empty(40, 95, dtype=torch.int8, **meta), s)

@@ -310,6 +310,17 @@ def test_modules_on_gpu(dev, golden_dir):
     assert torch.equal(m.weight_int8.cpu(), torch.from_numpy(d["weight_int8"]))
     assert torch.equal(m.scale.cpu(), torch.from_numpy(d["scale"]))
     assert torch.equal(m.weight_transposed.cpu(), torch.from_numpy(d["weight_transposed"]))
+    # the module holds N*K + 4N bytes of weight state on the device (no second,
+    # transposed copy); its saved state dict is the reference's byte for byte
+    assert sum(b.numel() * b.element_size() for b in m.buffers()) == 128 * 64 + 4 * 128
+    sd = m.state_dict()
+    assert list(sd) == ["weight_int8", "scale", "weight_transposed"]
+    for k in ("weight_int8", "scale", "weight_transposed"):
+        assert sd[k].cpu().numpy().tobytes() == np.ascontiguousarray(d[k]).tobytes(), k
+    m3 = Int8Linear(64, 128).to(dev)
+    m3.load_state_dict(sd)
+    m3.mark_quantized()
+    assert torch.equal(m3(torch.from_numpy(d["x"]).to(dev)), m(torch.from_numpy(d["x"]).to(dev)))
     x = torch.from_numpy(d["x"]).to(dev)
     y = m(x)
     assert y.shape == (2, 8, 128) and y.dtype == torch.float16

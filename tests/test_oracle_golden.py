@@ -138,3 +138,36 @@ def test_package_quantization_matches_oracle(dtype):
     q, s = quantize_weight_per_channel(w)
     qo, so = orc.quantize_weight_per_channel(w.numpy())
     assert np.array_equal(q.numpy(), qo) and np.array_equal(s.numpy(), so)
+
+
+def test_torch_restatement_matches_reference_vectors(golden_dir):
+    """The torch restatement of the reference's CPU route (the CPU baseline of
+    bench.py) reproduces the reference's own outputs bit for bit: it runs the
+    same torch ops as the reference on the same inputs."""
+    from oracle import torch_ref
+    d = _load(golden_dir, "ref_gemm_cases.npz")
+    for i in range(int(d["n_cases"])):
+        x = torch.from_numpy(d[f"c{i}_x"])
+        w = torch.from_numpy(d[f"c{i}_w"])
+        s = torch.from_numpy(d[f"c{i}_scale"])
+        b = torch.from_numpy(d[f"c{i}_bias"]) if bool(d[f"c{i}_has_bias"]) else None
+        y = torch_ref.int8_gemm_torch(x, w, s, b)
+        assert y.dtype == torch.float16
+        assert np.array_equal(y.numpy(), d[f"c{i}_y"]), f"case {i}"
+    d = _load(golden_dir, "ref_test_imports_gemm.npz")
+    y = torch_ref.int8_gemm_torch(torch.from_numpy(d["x"]), torch.from_numpy(d["w"]), torch.from_numpy(d["scale"]))
+    assert np.array_equal(y.numpy(), d["y"])
+    q = torch.from_numpy(_load(golden_dir, "ref_quantization.npz")["q_channel"])
+    s = torch.from_numpy(_load(golden_dir, "ref_quantization.npz")["s_channel"])
+    r = torch_ref.dequantize(q, s, dtype=torch.float32, dim=0)
+    assert np.array_equal(r.numpy(), _load(golden_dir, "ref_quantization.npz")["r_channel"])
+
+
+def test_torch_restatement_config0(golden_dir):
+    """Config 0 through the torch restatement: the reference's output, bit for bit."""
+    from oracle import torch_ref
+    from rotalabs_accel_b200.synthetic import make_problem
+    d = _load(golden_dir, "ref_config0.npz")
+    x, q, s = make_problem(32, 4096, 4096, seed=0)
+    y = torch_ref.int8_gemm_torch(x, q, s)
+    assert np.array_equal(y.numpy(), d["y"])
