@@ -352,12 +352,14 @@ def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, ar
     own GPU (``single_gpu_us``, same run, max over ranks), so that the line
     carries the strong-scaling efficiency t1 / (N * tN)."""
     import torch
-    from rotalabs_accel_b200.sharded import assemble_columns, shard_range
+    from rotalabs_accel_b200.sharded import assemble_columns, prefill_overlapped, shard_range
     out = {"workload": "BASELINE config 4: Llama-3-70B MLP GEMMs (8192->28672, 28672->8192), M in {1, 16, 4096}, "
                        f"column-parallel over {world} GPU(s); weights N(0, 0.02) per-channel int8, fp16 scales",
            "exchange": ("none (one GPU)" if world == 1 else
-                        "decode: peer-to-peer all-gather fused into the decode kernel; prefill: NCCL all-gather"
-                        if exchange is not None else "NCCL all-gather + column assembly"),
+                        ("decode: peer-to-peer all-gather fused into the decode kernel; "
+                         if exchange is not None else "decode: NCCL all-gather + column assembly; ")
+                        + "prefill: blocks of rows, each block's NCCL all-gather and column assembly on a "
+                          "communication stream overlapping the next block's GEMM"),
            "scaling": "strong",
            "parity_reference": "fp32-accumulated dequant-matmul of the full layer; tolerance |err| <= "
                                "1e-2 * max(1, |ref|) per element, every rank's assembled output"}
@@ -387,6 +389,8 @@ def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, ar
                         _capi.w8a16_gemm(x, q, sc, None, out=y)
                     elif exchange is not None and not prefill:
                         exchange.gemm(x, q, sc, None, out=y)
+                    elif prefill:
+                        prefill_overlapped(x, q, sc, None, world * n_local, world, out=y)
                     else:
                         _capi.w8a16_gemm(x, q, sc, None, out=y_local)
                         dist.all_gather_into_tensor(staging, y_local)

@@ -380,6 +380,17 @@ def ipc_close(ptr: int) -> None:
     _check(load_library().rla_ipc_close(ptr), "rla_ipc_close")
 
 
+_sm_counts: dict = {}
+
+
+def device_sm_count(index: int) -> int:
+    """Streaming multiprocessors of CUDA device ``index`` (cached)."""
+    n = _sm_counts.get(index)
+    if n is None:
+        n = _sm_counts[index] = torch.cuda.get_device_properties(index).multi_processor_count
+    return n
+
+
 def torch_op_loaded() -> bool:
     """Whether ``torch.ops.rla.w8a16_gemm`` is registered (``_rla_torch_ops.so``)."""
     load_library()

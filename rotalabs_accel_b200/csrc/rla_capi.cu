@@ -85,6 +85,17 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
   // 8192 -> 3584 9.1 -> 8.2 us; not at 11008 -> 4096 (12.0 -> 12.6 us).
   if (!gated && !peer && p.nt == 1 && p.wn == 1 && p.wk == 8 && (K >= 16384 || (K >= 8192 && N < 4096)))
     p.wk = 4;
+  // M <= 8 on layers of at most two row blocks per SM (but more than one):
+  // one 512-thread CTA of 16 k-warps per row block (two resident per SM),
+  // each warp's K share in fewer batches of loads, no split of K across CTAs
+  // (in place of two 256-thread CTAs in a cluster).  Measured on B200 at
+  // M = 1 (CUDA graphs): 4096 -> 4096 6.2 -> 5.1 us, 11008 -> 4096
+  // 12.0 -> 10.1 us; not in place of the long-K 128-thread plans above
+  // (8192 -> 3584: 8.2 -> 8.4 us).
+  if (!gated && !peer && p.nt == 1 && p.wn == 1 && p.wk == 8 && chunks >= 64) {
+    const int64_t r16 = skinny_resident_ctas(1, 1, 16, false, true, false, 1);
+    if (p.grid_x <= r16 && 2 * p.grid_x > r16) p.wk = 16;
+  }
   // M = 9..16 in 128-thread CTAs: loading each chunk's activations just
   // before its MMAs costs registers (fewer CTAs fit per SM) but streams
   // faster; used while the grid still fits in one wave.  Measured on B200,
@@ -238,7 +249,15 @@ static Plan make_plan_uncached(int64_t M, int64_t N, int64_t K, bool aligned, bo
   if (aligned && M > 32) {
     p.kernel = RLA_KERNEL_TCGEN05;
     const int64_t ntiles = (N + 127) / 128;
-    if (M >= 256 && ntiles * ((M + 255) / 256) >= sms) {
+    // Tile height by whole waves of tiles (one CTA per SM): 256-row tiles
+    // unless 128-row tiles finish in less time; a 128-row tile does half the
+    // work of a 256-row one at about 16 % less throughput per FLOP (B200:
+    // ~7.4 vs ~6.4 TFLOP/s per SM).
+    auto wave_cost = [&](int64_t bm, double rel) {
+      const int64_t tiles = ntiles * ((M + bm - 1) / bm);
+      return static_cast<double>((tiles + sms - 1) / sms) * static_cast<double>(bm) * rel;
+    };
+    if (M > 128 && wave_cost(256, 1.0) <= wave_cost(128, 1.16)) {
       p.bm = 256; p.stages = 4;
     } else if (M > 64) {
       p.bm = 128; p.stages = 6;

@@ -67,13 +67,12 @@ RLA_DEVFN void skinny_chunk_mma(float (&acc)[NT][4], const uint4 (&wa)[2], const
 }
 
 template <int NT, int WN, int WK, int U, bool PEER, bool GLU, bool XJ>
-__global__ void __launch_bounds__(32 * WN * WK)
-    w8a16_skinny_kernel(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,
-                        const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias,
-                        int bias_kind, __half* __restrict__ y, int64_t ldy, int M, int N, int K,
-                        int chunks_per_split, float* __restrict__ partial, unsigned int* __restrict__ counters,
-                        const __grid_constant__ PeerOut po, const int8_t* __restrict__ w_up,
-                        const void* __restrict__ scale_up, const void* __restrict__ bias_up) {
+RLA_DEVFN void skinny_body(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,
+                           const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias,
+                           int bias_kind, __half* __restrict__ y, int64_t ldy, int M, int N, int K,
+                           int chunks_per_split, float* __restrict__ partial, unsigned int* __restrict__ counters,
+                           const PeerOut& po, const int8_t* __restrict__ w_up, const void* __restrict__ scale_up,
+                           const void* __restrict__ bias_up) {
   static_assert(!(PEER && GLU), "the gated form has no peer exchange");
   constexpr int OUTS = GLU ? 8 * WN : 16 * WN;  // output channels per CTA
   const int lane = threadIdx.x & 31;
@@ -392,6 +391,30 @@ __global__ void __launch_bounds__(32 * WN * WK)
   if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
 }
 
+#define RLA_SKINNY_PARAMS                                                                                     \
+  const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,                         \
+      const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias, int bias_kind,               \
+      __half* __restrict__ y, int64_t ldy, int M, int N, int K, int chunks_per_split, float* __restrict__ partial, \
+      unsigned int* __restrict__ counters, const __grid_constant__ PeerOut po, const int8_t* __restrict__ w_up,   \
+      const void* __restrict__ scale_up, const void* __restrict__ bias_up
+#define RLA_SKINNY_ARGS                                                                                   \
+  x, ldx, w, ldw, scale, scale_f32, bias, bias_kind, y, ldy, M, N, K, chunks_per_split, partial, counters, po, \
+      w_up, scale_up, bias_up
+
+template <int NT, int WN, int WK, int U, bool PEER, bool GLU, bool XJ>
+__global__ void __launch_bounds__(32 * WN * WK) w8a16_skinny_kernel(RLA_SKINNY_PARAMS) {
+  skinny_body<NT, WN, WK, U, PEER, GLU, XJ>(RLA_SKINNY_ARGS);
+}
+
+// One row group of 16 k-warps (512 threads) with the register budget of two
+// resident CTAs per SM (64 registers): for M <= 8 on layers of at most two
+// row blocks per SM, every warp's K share is in flight in one batch of loads
+// and the slices add up in shared memory, with no split of K across CTAs.
+template <int NT, int U, bool XJ>
+__global__ void __launch_bounds__(512, 2) w8a16_skinny16_kernel(RLA_SKINNY_PARAMS) {
+  skinny_body<NT, 1, 16, U, false, false, XJ>(RLA_SKINNY_ARGS);
+}
+
 // ---------------------------------------------------------------------------
 // Host side.  Per-device facts about an instantiation (its dynamic
 // shared-memory attribute, its occupancy) are cached per device, lock-free:
@@ -416,9 +439,14 @@ struct SkinnyInst {
                          __half*, int64_t, int, int, int, int, float*, unsigned int*, const PeerOut, const int8_t*,
                          const void*, const void*);
   static KernT kernel(int form) {
-    return form == 1   ? w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>
-           : form == 2 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>
-                       : w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>;
+    if constexpr (WN * WK == 16) {
+      (void)form;  // plain form only (the plan never asks for the others)
+      return w8a16_skinny16_kernel<NT, U, XJ>;
+    } else {
+      return form == 1   ? w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>
+             : form == 2 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>
+                         : w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>;
+    }
   }
   // CTAs that can be resident on the whole device at once when the K slices
   // of a row block form clusters of `cluster` CTAs (1: no cluster).  With
@@ -514,6 +542,12 @@ static cudaError_t launch_cfg(const GemmArgs& a, const Plan& p, void* workspace,
 template <int NT>
 static cudaError_t launch_nt(const GemmArgs& a, const Plan& p, void* ws, cudaStream_t s) {
   if (p.wn == 1 && p.wk == 8) return launch_cfg<NT, 1, 8, NT == 1>(a, p, ws, s);
+  if constexpr (NT == 1) {
+    if (p.wn == 1 && p.wk == 16) {
+      if (a.w_up || a.peer.world > 0) return cudaErrorInvalidConfiguration;
+      return launch_cfg<NT, 1, 16, true>(a, p, ws, s);
+    }
+  }
   if (p.wn == 2 && p.wk == 4) return launch_cfg<NT, 2, 4, false>(a, p, ws, s);
   if (p.wn == 4 && p.wk == 2) return launch_cfg<NT, 4, 2, false>(a, p, ws, s);
   if (p.wn == 1 && p.wk == 4) {
@@ -528,6 +562,9 @@ static cudaError_t launch_nt(const GemmArgs& a, const Plan& p, void* ws, cudaStr
 template <int NT>
 static int resident_nt(int wn, int wk, int form, bool xjit, int cluster) {
   if (wn == 1 && wk == 8) return SkinnyInst<NT, 1, 8, NT == 1>::resident(form, cluster);
+  if constexpr (NT == 1) {
+    if (wn == 1 && wk == 16) return form == 0 ? SkinnyInst<NT, 1, 16, true>::resident(form, cluster) : 0;
+  }
   if (wn == 2 && wk == 4) return SkinnyInst<NT, 2, 4, false>::resident(form, cluster);
   if (wn == 4 && wk == 2) return SkinnyInst<NT, 4, 2, false>::resident(form, cluster);
   if (wn == 1 && wk == 4) {

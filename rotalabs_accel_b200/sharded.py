@@ -13,6 +13,9 @@ Forward, per rank, collective path:
      ``staging[world, M, n_local]`` (NCCL over NVLink on GPUs, gloo on the CPU);
   3. ``rla_gather_columns`` reorders the staging buffer into ``y[M, N]``
      (skipped when M == 1: the staging layout already is ``[1, N]``).
+On GPUs a long prefill (``prefill_overlapped``) runs these steps per block
+of rows: the all-gather and reorder of block i run on a communication stream
+while the GEMM of block i+1 runs, so the exchange hides behind the math.
 
 Fused path (after ``enable_peer_exchange``; decode batches of at most
 ``max_tokens`` rows, K % 16 == 0): one kernel per rank computes its slice,
@@ -72,6 +75,93 @@ def assemble_columns(staging: torch.Tensor, n_total: int, out: Optional[torch.Te
     if out is None:
         return y.contiguous()
     out.copy_(y)
+    return out
+
+
+# Block sizes of the overlapped prefill, from a two-stream pipeline model:
+# the local GEMM of a block takes whole waves of tiles (tcgen05 kernel, one
+# tile per SM at a time), and the all-gather plus reorder of a block runs
+# while the next block's GEMM does.  Figures measured on B200: about
+# 7.4 TFLOP/s per SM for 256-row tiles and 6.4 for 128-row tiles; the NCCL
+# all-gather delivers about 650 GB/s into each rank; the reorder moves about
+# 5 TB/s.
+def _gemm_us(rows: int, n_local: int, K: int, sms: int) -> float:
+    nt = -(-n_local // 128)
+
+    def waves(bm):
+        return -(-(nt * -(-rows // bm)) // sms)
+
+    # the library's own choice of tile height (rla_capi.cu, make_plan)
+    bm = 256 if rows > 128 and waves(256) * 256 * 1.0 <= waves(128) * 128 * 1.16 else 128
+    rate = 7.4e12 if bm == 256 else 6.4e12
+    return waves(bm) * (2.0 * 128 * bm * K / rate) * 1e6
+
+
+def prefill_row_blocks(M: int, n_local: int, K: int = 8192, world: int = 2, sms: int = 148):
+    """``[(row0, rows), ...]`` covering ``[0, M)`` (blocks of equal size, a
+    multiple of 128 rows, but the last): of the splits into about 1, 2, 4 or
+    8 blocks, the one with the least modelled time; 1 block is the serial
+    GEMM -> all-gather -> reorder."""
+    best, best_t = None, None
+    for c in (1, 2, 4, 8):
+        rows = -(-M // c)
+        rows = -(-rows // 128) * 128
+        blocks, r0 = [], 0
+        while r0 < M:
+            blocks.append((r0, min(rows, M - r0)))
+            r0 += rows
+        t_gemm = t_comm = 0.0
+        for _, r in blocks:
+            t_gemm += _gemm_us(r, n_local, K, sms)
+            ag = 15.0 + (world - 1) * r * n_local * 2 / 650e9 * 1e6
+            reorder = 2.0 * r * world * n_local * 2 / 5e12 * 1e6
+            t_comm = max(t_gemm, t_comm) + ag + reorder
+        if best_t is None or t_comm < best_t * 0.97:   # more blocks only for a clear gain
+            best, best_t = blocks, t_comm
+    return best
+
+
+_comm_streams: dict = {}
+
+
+def prefill_overlapped(x2: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
+                       bias: Optional[torch.Tensor], n_total: int, world: int, group=None,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Column-parallel W8A16 GEMM of a long activation block on CUDA:
+    ``y[M, n_total]`` on every rank from its shard ``weight_int8 [n_local, K]``.
+
+    Per block of rows (``prefill_row_blocks``): the local GEMM on the current
+    stream, then, on a per-device communication stream that waits for it, the
+    NCCL all-gather of the block's slices and their reorder into the block's
+    rows of ``y``.  The GEMM of the next block runs meanwhile.  The current
+    stream waits for the communication stream before returning, so the
+    result is ordered like any other stream work (also under CUDA-graph
+    capture).  Every rank makes the same calls in the same order."""
+    M, K = x2.shape
+    n_local = weight_int8.shape[0]
+    dev = x2.device
+    if out is None:
+        out = torch.empty((M, n_total), dtype=torch.float16, device=dev)
+    cur = torch.cuda.current_stream(dev)
+    comm = _comm_streams.get(dev.index)
+    if comm is None:
+        comm = _comm_streams[dev.index] = torch.cuda.Stream(device=dev)
+    from . import _capi
+    blocks = prefill_row_blocks(M, n_local, K, world, _capi.device_sm_count(dev.index))
+    # every buffer is allocated here on the current stream and lives until
+    # the communication stream has been joined back (no cross-stream frees)
+    staging = torch.empty((world * M * n_local,), dtype=torch.float16, device=dev)   # [world, rows, n_local] per block
+    y_loc = torch.empty((M, n_local), dtype=torch.float16, device=dev)
+    for r0, rows in blocks:
+        _capi.w8a16_gemm(x2[r0:r0 + rows], weight_int8, scale, bias, out=y_loc[r0:r0 + rows])
+        done = torch.cuda.Event()
+        done.record(cur)
+        with torch.cuda.stream(comm):
+            comm.wait_event(done)
+            st = staging[world * r0 * n_local:world * (r0 + rows) * n_local].view(world, rows, n_local)
+            dist.all_gather_into_tensor(st, y_loc[r0:r0 + rows], group=group)
+            assemble_columns(st, n_total, out=out[r0:r0 + rows])
+    cur.wait_stream(comm)
     return out
 
 
@@ -183,6 +273,16 @@ class ColumnParallelInt8Linear(torch.nn.Module):
             if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
                 x2 = x2.clone(memory_format=torch.contiguous_format)
             y = self._exchange.gemm(x2, self.weight_int8, self.scale, self.bias)
+            if y.shape[1] != self.out_features:
+                y = y[:, :self.out_features]
+            return y.reshape(*lead, self.out_features)
+        if (self.world > 1 and x2.is_cuda and M >= 1024 and x2.dtype == torch.float16 and x2.stride(1) == 1
+                and self.weight_int8.stride(1) == 1):
+            b = self.bias
+            if b is not None and b.dtype not in (torch.float16, torch.float32):
+                b = b.half()
+            y = prefill_overlapped(x2, self.weight_int8, self.scale, b, self.world * self.n_local, self.world,
+                                   group=self.group)
             if y.shape[1] != self.out_features:
                 y = y[:, :self.out_features]
             return y.reshape(*lead, self.out_features)

@@ -92,6 +92,30 @@ def test_world1_fused_equals_plain(single_rank_group, kernel):
         _capi.set_decode_kernel("auto")
 
 
+def test_world1_fused_cluster_grid_at_residency_estimate(single_rank_group):
+    """A skinny exchange launch whose row blocks (74 of 16 rows) times its
+    cluster split of K would fill the per-SM residency estimate exactly
+    (74 x 8 = 592 CTAs at 4 per SM): its plan counts residency in whole
+    clusters, so the grid it launches fits at once and every wait ends
+    (no device error)."""
+    from rotalabs_accel_b200 import _capi
+    from rotalabs_accel_b200.peer import PeerExchange
+    _capi.set_decode_kernel("skinny")
+    ex = PeerExchange(max_rows=32, max_n_local=8192)
+    try:
+        for M, N, K in ((1, 74 * 16, 8192), (4, 74 * 16, 16384), (1, 37 * 16, 28672)):
+            x, q, s, b = _problem(M, N, K, 300 + M)
+            ref = _capi.w8a16_gemm(x, q, s, b)
+            for _ in range(3):
+                y = ex.gemm(x, q, s, b)
+            torch.cuda.synchronize()
+            assert _close(y, ref), (M, N, K)
+        assert _capi.device_error() == 0
+    finally:
+        ex.close()
+        _capi.set_decode_kernel("auto")
+
+
 def test_world1_fused_under_graph_replay(single_rank_group):
     from rotalabs_accel_b200 import _capi
     from rotalabs_accel_b200.peer import PeerExchange
@@ -178,7 +202,7 @@ def _worker_multi(rank, world, port, q):
         from rotalabs_accel_b200 import _capi, int8_gemm_torch, quantize_weight_per_channel
         from rotalabs_accel_b200.peer import PeerExchange
         from rotalabs_accel_b200.sharded import ColumnParallelInt8Linear
-        ex = PeerExchange(max_rows=16, max_n_local=-(-14336 // world))
+        ex = PeerExchange(max_rows=16, max_n_local=-(-28672 // world))
         report = []
         ok = True
         for kernel in ("auto", "skinny", "stream"):
@@ -214,6 +238,54 @@ def _worker_multi(rank, world, port, q):
                         ok = False
                         report.append((kernel, M, K, N, it, same, err))
         _capi.set_decode_kernel("auto")
+        # The benchmark's config 4 shards (Llama-3-70B MLP GEMMs, column-parallel
+        # over the world): the fused exchange and the NCCL path both against the
+        # fp32 dequant-matmul of the full layer.  The full weight is made on
+        # every rank's device from the same seed.
+        for (M, K, N) in [(1, 8192, 28672), (16, 8192, 28672), (1, 28672, 8192), (16, 28672, 8192)]:
+            g = torch.Generator(device=dev).manual_seed(70 + M + K)
+            W = torch.randn(N, K, generator=g, device=dev) * 0.02
+            m_nccl = ColumnParallelInt8Linear(K, N).to(dev)
+            m_nccl.quantize_weights(W)
+            m_p2p = ColumnParallelInt8Linear(K, N).to(dev)
+            m_p2p.load_state_dict(m_nccl.state_dict())
+            m_p2p._quantized = True
+            m_p2p.enable_peer_exchange(max_tokens=16, exchange=ex)
+            wq, s = quantize_weight_per_channel(W)
+            del W
+            for it in range(2):
+                x = torch.randn(M, K, generator=g, device=dev).half()
+                y_p2p = m_p2p(x)
+                y_nccl = m_nccl(x)
+                ref = x.float() @ (wq.float() * s.float()[:, None]).t()
+                torch.cuda.synchronize()
+                tol = 1e-2 * max(1.0, float(ref.abs().max()))
+                e_p2p = float((y_p2p.float() - ref).abs().max())
+                e_nccl = float((y_nccl.float() - ref).abs().max())
+                if e_p2p > tol or e_nccl > tol:
+                    ok = False
+                    report.append(("config4", M, K, N, it, e_p2p, e_nccl))
+            del m_nccl, m_p2p, wq, s
+            torch.cuda.empty_cache()
+        # Long prefill blocks take the overlapped path (row blocks, each block's
+        # all-gather on a communication stream behind the next block's GEMM).
+        for (M, K, N) in [(1024, 8192, 28672), (2048, 28672, 8192)]:
+            g = torch.Generator(device=dev).manual_seed(90 + K)
+            W = torch.randn(N, K, generator=g, device=dev) * 0.02
+            m = ColumnParallelInt8Linear(K, N).to(dev)
+            m.quantize_weights(W)
+            wq, s = quantize_weight_per_channel(W)
+            del W
+            x = torch.randn(M, K, generator=g, device=dev).half()
+            y = m(x)
+            ref = x.float() @ (wq.float() * s.float()[:, None]).t()
+            torch.cuda.synchronize()
+            err = float((y.float() - ref).abs().max())
+            if err > 1e-2 * max(1.0, float(ref.abs().max())):
+                ok = False
+                report.append(("prefill overlapped", M, K, N, err))
+            del m, wq, s, x, y, ref
+            torch.cuda.empty_cache()
         # graph replay of several layers sharing the exchange
         layers = []
         for i, (M, K, N) in enumerate([(1, 4096, 4096), (8, 4096, 11008), (16, 4096, 14336)]):
@@ -256,7 +328,7 @@ def _worker_multi(rank, world, port, q):
         q.put((rank, False, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_multi_gpu_fused_equals_nccl_path(cuda_lib, world):
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:

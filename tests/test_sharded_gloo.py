@@ -154,3 +154,22 @@ def _worker_dead_peer(rank, world, port, q):
 def test_dead_peer_is_detected_not_hung():
     res = _run(_worker_dead_peer, 2, timeout=90)
     assert all(r[1] for r in res), res
+
+
+def test_prefill_row_blocks_cover_rows():
+    """The overlapped prefill's row blocks tile [0, M) in order, in equal
+    multiples of 128 rows (but the last), at most 8 of them; a narrow
+    shard whose whole GEMM is one wave is split in two so that the exchange
+    of the first half hides behind the second half's GEMM."""
+    from rotalabs_accel_b200.sharded import prefill_row_blocks
+    for M in (1024, 1500, 2048, 4096, 4097):
+        for n_local, K, world in ((3584, 8192, 8), (1024, 28672, 8), (14336, 8192, 2), (7168, 8192, 4)):
+            blocks = prefill_row_blocks(M, n_local, K, world)
+            assert 1 <= len(blocks) <= 8
+            r = 0
+            for (r0, rows) in blocks:
+                assert r0 == r and rows > 0
+                r += rows
+            assert r == M
+            assert all(rows % 128 == 0 for _, rows in blocks[:-1])
+    assert len(prefill_row_blocks(4096, 1024, 28672, 8)) == 2

@@ -72,8 +72,12 @@ def test_no_alloc_matches_workspace_entry_point():
     lib = _lib()
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    # split-K plans of several shapes (the scratch is really used) and one
-    # without split-K
+    # split-K plans of several shapes and one without split-K; the first
+    # needs more than 8 K slices, so its partial sums really go through the
+    # static scratch (not through a thread-block cluster)
+    from rotalabs_accel_b200 import _capi
+    assert lib.rla_w8a16_workspace_size(8, 1024, 28672) > 0
+    assert _capi.plan(8, 1024, 28672)["splits"] > 8
     for i, (M, N, K) in enumerate([(8, 1024, 28672), (16, 1024, 4096), (1, 512, 8192), (4, 14336, 4096)]):
         x, q, s, b = _problem(M, N, K, 100 + i, dev)
         y_ws = _with_workspace(lib, x, q, s, b, stream)
