@@ -89,11 +89,12 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def load_traffic():
-    """Per-launch DRAM bytes (read + write) of the decode kernel over the sweep:
-    the mean of one ncu capture of the 16 launches (profiles/decode_sweep_traffic.json
-    holds the figure and the command that measured it)."""
-    p = os.path.join(ROOT, "profiles", "decode_sweep_traffic.json")
+def load_traffic(name="decode_sweep_traffic.json"):
+    """Per-launch DRAM bytes (read + write) from one ncu capture: the decode
+    kernel's mean over the sweep's 16 launches, or one config 2 prefill
+    launch (the JSON files under profiles/ hold the figure and the command
+    that measured it)."""
+    p = os.path.join(ROOT, "profiles", name)
     try:
         return float(json.load(open(p))["traffic_bytes_per_launch"])
     except (OSError, ValueError, KeyError, TypeError):
@@ -673,36 +674,66 @@ def main():
                          x_ready=torch.cuda.Event(), y_ready=torch.cuda.Event(), y_read=torch.cuda.Event()))
     copy_stream = torch.cuda.Stream(device=dev)
 
-    def e2e_step(i):
-        bf = bufs[i % 2]
-        with torch.cuda.stream(copy_stream):
-            if i >= 2:
-                copy_stream.wait_event(bf["y_read"])       # (its x is free once its GEMMs ran)
-            bf["x"].copy_(x_host_all, non_blocking=True)
-            bf["x_ready"].record(copy_stream)
-        with torch.cuda.stream(stream):
-            stream.wait_event(bf["x_ready"])
-            outs = [m(xd).view(-1) for m, xd in zip(mods, bf["views"])]
-            torch.cat(outs, out=bf["y"])
-            bf["y_ready"].record(stream)
-        with torch.cuda.stream(copy_stream):
-            copy_stream.wait_event(bf["y_ready"])
-            y_host_all[i % 2].copy_(bf["y"], non_blocking=True)
-            bf["y_read"].record(copy_stream)
+    # The step's two copies are issued as plain cudaMemcpyAsync calls on the
+    # copy stream (torch's copy_ from pinned memory also records an event in
+    # its host allocator per call, tens of microseconds of host time per step
+    # on this loop).
+    import ctypes
+    cudart = None
+    for name in ("libcudart.so.12", "libcudart.so"):
+        try:
+            cudart = ctypes.CDLL(name)
+            break
+        except OSError:
+            continue
+    cudart.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                       ctypes.c_void_p]
+    cudart.cudaMemcpyAsync.restype = ctypes.c_int
+    H2D, D2H = 1, 2
+    x_bytes = x_host_all.numel() * 2
+    y_bytes = y_host_all[0].numel() * 2
+    cs = copy_stream.cuda_stream
 
-    for i in range(3):
-        e2e_step(i)
+    def memcpy(dst, src, n, kind):
+        st = cudart.cudaMemcpyAsync(dst, src, n, kind, cs)
+        if st != 0:
+            raise RuntimeError(f"cudaMemcpyAsync failed with status {st}")
+
+    def e2e_run(steps, timed_events=None):
+        """`steps` steps through the public API.  The compute stream stays
+        current; each step has its read-back and the input copy of step i+2
+        on the copy stream, into the buffer set step i has finished with
+        (steps 0 and 1 copy theirs first).  Every step's input and result
+        copies are inside the region."""
+        with torch.cuda.stream(stream):
+            if timed_events:
+                timed_events[0].record(stream)
+            copy_stream.wait_stream(stream)
+            for j in range(min(2, steps)):
+                memcpy(bufs[j]["x"].data_ptr(), x_host_all.data_ptr(), x_bytes, H2D)
+                bufs[j]["x_ready"].record(copy_stream)
+            for i in range(steps):
+                bf = bufs[i % 2]
+                stream.wait_event(bf["x_ready"])
+                outs = [m(xd).view(-1) for m, xd in zip(mods, bf["views"])]
+                torch.cat(outs, out=bf["y"])
+                bf["y_ready"].record(stream)
+                copy_stream.wait_event(bf["y_ready"])
+                memcpy(y_host_all[i % 2].data_ptr(), bf["y"].data_ptr(), y_bytes, D2H)
+                if i + 2 < steps:
+                    memcpy(bf["x"].data_ptr(), x_host_all.data_ptr(), x_bytes, H2D)
+                    bf["x_ready"].record(copy_stream)
+            stream.wait_stream(copy_stream)
+            if timed_events:
+                timed_events[1].record(stream)
+
+    e2e_run(3)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    copy_stream.wait_event(e0)
-    for i in range(args.e2e_steps):
-        e2e_step(i)
-    stream.wait_stream(copy_stream)
-    e1.record(stream)
+    e2e_run(args.e2e_steps, (e0, e1))
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / args.e2e_steps
     if world > 1:
@@ -733,7 +764,9 @@ def main():
                    "steps": pre_steps, "gemms": [f"{PREFILL_M}x{K}->{N}" for (K, N) in PREFILL_KN],
                    "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["bf16_tflops"],
                                 "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4),
-                                "peak_kind": f"dense bf16/fp16 burst ({peaks['source']})", "traffic": None},
+                                "peak_kind": f"dense bf16/fp16 burst ({peaks['source']})",
+                                "traffic": load_traffic("prefill_traffic.json"),
+                                "traffic_launch": "M=2048, K=4096, N=11008, w8a16_tc_kernel<256, 4>"},
                    "clocks": pclocks}
         del g_pre
 
@@ -786,8 +819,8 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
                     "path": "Int8Linear.forward (public API), eager; per step one pinned host -> device copy "
                             "of all 16 inputs, and all 16 outputs read back in one device -> pinned host copy; "
-                            "copies on a copy stream with two device buffer sets (step i+1's input and step i's "
-                            "result copies overlap the GEMMs)"
+                            "copies on a copy stream with two device buffer sets (a step's inputs are copied two "
+                            "steps ahead, its results read back right after it; both overlap other steps' GEMMs)"
                             + ("" if world == 1 else "; on every GPU, max over ranks")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,

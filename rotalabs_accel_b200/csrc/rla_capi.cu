@@ -179,28 +179,37 @@ static void stream_shape(Plan& p, int64_t M, int64_t N, int64_t K, int sms) {
 static Plan make_plan_uncached(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace, bool peer);
 
 // The plan depends only on the shape, the flags, the device (its SM count and
-// occupancy) and the forced decode kernel; a call usually asks twice in a row
-// (workspace size, then the launch), so each host thread keeps its last plan.
+// occupancy) and the forced decode kernel.  A model calls a few shapes over
+// and over, each twice in a row (workspace size, then the launch), so each
+// host thread keeps its recent plans in a small direct-mapped cache.
 Plan make_plan(int64_t M, int64_t N, int64_t K, bool aligned, bool have_workspace, bool peer) {
-  struct Key {
-    int64_t M, N, K;
-    int dev, flags, choice;
+  struct Entry {
+    int64_t M = -1, N = -1, K = -1;
+    int dev = -1, flags = -1, choice = -1;
+    Plan plan;
   };
-  thread_local Key last{-1, -1, -1, -1, -1, -1};
-  thread_local Plan last_plan;
+  constexpr int kEntries = 32;
+  thread_local Entry cache[kEntries];
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
   const int flags = (aligned ? 1 : 0) | (have_workspace ? 2 : 0) | (peer ? 4 : 0);
   const int choice = g_decode_kernel.load(std::memory_order_relaxed);
+  const uint64_t h = (static_cast<uint64_t>(M) * 0x9E3779B97F4A7C15ull) ^ (static_cast<uint64_t>(N) * 0xC2B2AE3D27D4EB4Full) ^
+                     (static_cast<uint64_t>(K) * 0x165667B19E3779F9ull) ^ static_cast<uint64_t>(flags * 7 + dev * 131);
+  Entry& e = cache[(h >> 32) % kEntries];
 #ifndef RLA_EXPERIMENTS  // (experiment builds read plan overrides from the environment on every call)
-  if (dev >= 0 && last.M == M && last.N == N && last.K == K && last.dev == dev && last.flags == flags &&
-      last.choice == choice)
-    return last_plan;
+  if (dev >= 0 && e.M == M && e.N == N && e.K == K && e.dev == dev && e.flags == flags && e.choice == choice)
+    return e.plan;
 #endif
   const Plan p = make_plan_uncached(M, N, K, aligned, have_workspace, peer);
   if (dev >= 0) {
-    last = Key{M, N, K, dev, flags, choice};
-    last_plan = p;
+    e.M = M;
+    e.N = N;
+    e.K = K;
+    e.dev = dev;
+    e.flags = flags;
+    e.choice = choice;
+    e.plan = p;
   }
   return p;
 }
