@@ -336,16 +336,18 @@ def _sharded_parity(dist, world, x, q, sc, y, prefill):
     return float(out[0]), float(out[1]), int(ref.shape[0])
 
 
-def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, args, exchange):
+def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, args, exchange, pexchange=None):
     """Config 4: the Llama-3-70B MLP GEMMs (K=8192 -> N=28672, K=28672 ->
     N=8192) column-parallel over the world's GPUs.  Each rank holds its
     N / world output channels.  Decode (M = 1, 16): the fused peer-exchange
     launch (``--exchange p2p``) or the local GEMM + NCCL all-gather + column
     assembly (``--exchange nccl``); one GPU: the plain GEMM.  A decode step
     runs the GEMM on several copies of the weight shard, together larger than
-    3 x L2, so nothing is re-read from L2.  Prefill (M = 4096): the local
-    tcgen05 GEMM, then the NCCL all-gather and assembly (one weight copy: the
-    GEMM is compute-bound).  Times are device-side, max over ranks; values are
+    3 x L2, so nothing is re-read from L2.  Prefill (M = 4096, one weight
+    copy: the GEMM is compute-bound): row blocks of the local tcgen05 GEMM,
+    each block pulled from every rank over NVLink by ``PrefillExchange``
+    (``--exchange p2p``) or all-gathered with NCCL and reordered
+    (``--exchange nccl``) behind the next block's GEMM.  Times are device-side, max over ranks; values are
     whole-job (the full layer's algorithmic bytes or FLOPs / time).
 
     Every shape's assembled output is checked after its timed replays
@@ -359,8 +361,11 @@ def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, ar
            "exchange": ("none (one GPU)" if world == 1 else
                         ("decode: peer-to-peer all-gather fused into the decode kernel; "
                          if exchange is not None else "decode: NCCL all-gather + column assembly; ")
-                        + "prefill: blocks of rows, each block's NCCL all-gather and column assembly on a "
-                          "communication stream overlapping the next block's GEMM"),
+                        + ("prefill: blocks of rows; each block's slices pulled from every rank's exchange "
+                           "buffer over NVLink into the output's columns on a communication stream, "
+                           "overlapping the next block's GEMM" if pexchange is not None else
+                           "prefill: blocks of rows, each block's NCCL all-gather and column assembly on a "
+                           "communication stream overlapping the next block's GEMM")),
            "scaling": "strong",
            "parity_reference": "fp32-accumulated dequant-matmul of the full layer; tolerance |err| <= "
                                "1e-2 * max(1, |ref|) per element, every rank's assembled output"}
@@ -390,6 +395,8 @@ def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, ar
                         _capi.w8a16_gemm(x, q, sc, None, out=y)
                     elif exchange is not None and not prefill:
                         exchange.gemm(x, q, sc, None, out=y)
+                    elif prefill and pexchange is not None:
+                        pexchange.gemm(x, q, sc, None, out=y)
                     elif prefill:
                         prefill_overlapped(x, q, sc, None, world * n_local, world, out=y)
                     else:
@@ -558,7 +565,7 @@ def main():
 
     import rotalabs_accel_b200 as ra
     from rotalabs_accel_b200 import _capi
-    from rotalabs_accel_b200.peer import PeerExchange
+    from rotalabs_accel_b200.peer import PeerExchange, PrefillExchange
 
     peaks = load_peaks()
 
@@ -578,7 +585,7 @@ def main():
     torch.cuda.synchronize()
     bytes_step = sum(gemm_bytes(M, K, N) for (M, K, N) in jobs)
     p2p = world > 1 and args.exchange == "p2p"
-    exchange = None
+    exchange = pexchange = None
 
     stream = torch.cuda.Stream(device=dev)
 
@@ -778,9 +785,11 @@ def main():
     # ---- config 4: the 70B MLP GEMMs, column-parallel over the GPUs ----
     sharded = None
     if not args.no_sharded:
-        exchange = PeerExchange(max_rows=max(SHARDED_DECODE_M),
-                                max_n_local=max(-(-N // world) for (_, N) in SHARDED_KN)) if p2p else None
-        sharded = measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, args, exchange)
+        nl_max = max(-(-N // world) for (_, N) in SHARDED_KN)
+        exchange = PeerExchange(max_rows=max(SHARDED_DECODE_M), max_n_local=nl_max) if p2p else None
+        pexchange = PrefillExchange(max_rows=SHARDED_PREFILL_M, max_n_local=nl_max) if p2p else None
+        sharded = measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, args, exchange,
+                                  pexchange)
 
     # ---- CPU baseline (rank 0, N = 1) ----
     cpu = None
@@ -838,6 +847,8 @@ def main():
     torch.cuda.synchronize()
     if exchange is not None:
         exchange.close()
+    if pexchange is not None:
+        pexchange.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

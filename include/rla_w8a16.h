@@ -249,6 +249,53 @@ RLA_API int rla_ipc_open(const void* handle, void** ptr);
 RLA_API int rla_ipc_close(void* ptr);
 
 /*
+ * Pull exchange of the column-parallel prefill: the output step of a sharded
+ * Int8Linear (src/rotalabs_accel/kernels/gemm.py:241-336 with its output
+ * channels split over the ranks; rotalabs-accel itself has no distributed
+ * code) for long activation blocks, overlapped with the GEMM block by block.
+ * Rank r owns output columns [r * n_local, (r + 1) * n_local).
+ *
+ * Per rank, set up once (collectively): an exchange buffer xb of
+ * max_rows * ld_xb fp16 and a sync area of RLA_PX_SYNC_BYTES, both from
+ * rla_peer_alloc (zeroed), both IPC-mapped into every other rank.  One call:
+ *
+ *   rla_prefill_exchange_begin(sync_peers, rank, world, stream)
+ *       advances the call number and waits until every peer finished reading
+ *       this rank's xb in the previous call (so the GEMMs may overwrite it);
+ *   then for each block b = 0, 1, ... of rows [row0, row0 + rows):
+ *     rla_w8a16_gemm(... , y = xb + row0 * ld_xb, ldy = ld_xb, M = rows,
+ *                    N = n_local ...)               on the compute stream;
+ *     rla_prefill_exchange_block(xb_peers, ld_xb, sync_peers, rank, world,
+ *                    b, last = (b is the final block), row0, rows, n_local,
+ *                    y, ldy, comm_stream)           ordered after that GEMM
+ *       marks block b ready in every rank's sync area, waits for every
+ *       rank's mark of block b, and copies every rank's slice of those rows
+ *       from its xb (over NVLink) into y[row0:row0+rows, src * n_local ...].
+ *       On the last block it then tells every peer that this rank's reads of
+ *       the call are over.
+ *
+ * xb_peers / sync_peers are HOST arrays of `world` device pointers valid in
+ * this process (entry `rank` is this rank's own).  Needs n_local, ld_xb and
+ * ldy multiples of 8, ld_xb >= n_local, ldy >= world * n_local, 16-byte
+ * aligned xb and y, 128-byte aligned sync areas, block < RLA_PX_MAX_BLOCKS,
+ * rows < 2^31 (else RLA_ERR_INVALID_ARGUMENT, nothing launched).
+ * Every rank makes the same calls with the same blocks in the same order.
+ * Waits are bounded (rla_set_peer_wait_limit); a wait that gives up records
+ * device error 7 and marks the sync area (word RLA_PX_SYNC_ABORT_WORD); later
+ * calls on it record device error 9 and return at once, y incomplete.  The
+ * GEMMs themselves do not read the mark: after a failure every rank frees
+ * and re-creates its buffers.  Plain loads and stores over NVLink, no
+ * multicast, no copy engine.
+ */
+#define RLA_PX_SYNC_BYTES 1024
+#define RLA_PX_MAX_BLOCKS 16
+#define RLA_PX_SYNC_ABORT_WORD 1
+RLA_API int rla_prefill_exchange_begin(void* const* sync_peers, int rank, int world, void* stream);
+RLA_API int rla_prefill_exchange_block(const void* const* xb_peers, int64_t ld_xb, void* const* sync_peers, int rank,
+                                       int world, int block, int last, int64_t row0, int64_t rows, int64_t n_local,
+                                       void* y, int64_t ldy, void* stream);
+
+/*
  * Gate and up projections of a SwiGLU MLP in one W8A16 GEMM, with the
  * activation in the epilogue:
  *

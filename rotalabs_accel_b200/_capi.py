@@ -38,13 +38,16 @@ EXPORTED_SYMBOLS = (
     "rla_set_decode_kernel", "rla_w8a16_gemm_allgather", "rla_set_peer_wait_limit", "rla_peer_alloc",
     "rla_peer_free", "rla_ipc_export", "rla_ipc_open", "rla_ipc_close",
     "rla_w8a16_gemm_swiglu", "rla_w8a16_swiglu_workspace_size", "rla_rmsnorm",
-    "rla_w8a16_allgather_workspace_size",
+    "rla_w8a16_allgather_workspace_size", "rla_prefill_exchange_begin", "rla_prefill_exchange_block",
 )
 
 MAX_PEERS = 8
 PEER_SYNC_BYTES = 512
 PEER_SYNC_ABORT_WORD = 96
 IPC_HANDLE_BYTES = 64
+PX_SYNC_BYTES = 1024
+PX_MAX_BLOCKS = 16
+PX_SYNC_ABORT_WORD = 1
 
 _lib = None
 _fast = None
@@ -116,6 +119,11 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.rla_rmsnorm.restype = ctypes.c_int
         lib.rla_w8a16_allgather_workspace_size.argtypes = [i64, i64, i64]
         lib.rla_w8a16_allgather_workspace_size.restype = sz
+        lib.rla_prefill_exchange_begin.argtypes = [p, ctypes.c_int, ctypes.c_int, p]
+        lib.rla_prefill_exchange_begin.restype = ctypes.c_int
+        lib.rla_prefill_exchange_block.argtypes = [p, i64, p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                   i64, i64, i64, p, i64, p]
+        lib.rla_prefill_exchange_block.restype = ctypes.c_int
         if os.path.abspath(path) == LIB_PATH:
             # linked to this library by soname: the loader reuses the copy
             # loaded above, so both bindings share one library state
@@ -343,6 +351,29 @@ def w8a16_gemm_allgather(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: to
             ws_ptr, ws_bytes, stream)
     _check(st, "rla_w8a16_gemm_allgather")
     return out
+
+
+def prefill_exchange_begin(sync_ptrs, rank: int, stream: int) -> None:
+    """Start of one pull-exchange call (``rla_prefill_exchange_begin``):
+    advance the call number, wait until every peer finished reading this
+    rank's exchange buffer in the previous call.  ``sync_ptrs``: every rank's
+    sync area as mapped in this process."""
+    world = len(sync_ptrs)
+    syncs = (ctypes.c_void_p * world)(*sync_ptrs)
+    _check(load_library().rla_prefill_exchange_begin(syncs, rank, world, stream), "rla_prefill_exchange_begin")
+
+
+def prefill_exchange_block(xb_ptrs, ld_xb: int, sync_ptrs, rank: int, block: int, last: bool, row0: int, rows: int,
+                           n_local: int, out: torch.Tensor, stream: int) -> None:
+    """One block of the pull exchange (``rla_prefill_exchange_block``): mark
+    this rank's block ready everywhere, wait for every rank's, copy every
+    rank's slice of rows ``[row0, row0 + rows)`` into ``out``'s columns."""
+    world = len(xb_ptrs)
+    xbs = (ctypes.c_void_p * world)(*xb_ptrs)
+    syncs = (ctypes.c_void_p * world)(*sync_ptrs)
+    _check(load_library().rla_prefill_exchange_block(xbs, ld_xb, syncs, rank, world, block, 1 if last else 0, row0,
+                                                     rows, n_local, out.data_ptr(), out.stride(0), stream),
+           "rla_prefill_exchange_block")
 
 
 def set_peer_wait_limit(seconds: float) -> None:

@@ -7,3 +7,4 @@
 #include "rla_capi.cu"
 #include "rla_noalloc.cu"
 #include "rla_peer.cu"
+#include "rla_xchg.cu"

@@ -176,3 +176,148 @@ class PeerExchange:
         dist.barrier(group=self.group)       # no rank maps another's buffer any more
         self._recv.release()
         self._recv = None
+
+
+class _CudaArray:
+    """Minimal ``__cuda_array_interface__`` over a raw device pointer, so a
+    buffer of the library's own allocation can be viewed as a tensor."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _device_view(ptr: int, shape, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    typestr = {torch.float16: "<f2", torch.int32: "<i4"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device=device)
+
+
+_comm_streams: dict = {}
+
+
+def comm_stream(device: torch.device) -> torch.cuda.Stream:
+    """The per-device stream that the overlapped prefill runs its exchange on."""
+    s = _comm_streams.get(device.index)
+    if s is None:
+        s = _comm_streams[device.index] = torch.cuda.Stream(device=device)
+    return s
+
+
+class PrefillExchange:
+    """Exchange buffers and sync areas of a process group for the pull
+    exchange of the column-parallel prefill (``rla_prefill_exchange_*``):
+    calls of up to ``max_rows`` rows and ``max_n_local`` output columns per
+    rank, ``max_n_local`` a multiple of 8.
+
+    One call (``gemm``), on every rank in the same order with the same
+    shapes: the rows are cut into blocks; per block, this rank's GEMM writes
+    its slice into its own exchange buffer on the current stream, and on a
+    communication stream the pull kernel marks the block ready on every rank,
+    waits for every rank's mark and copies every rank's slice of those rows
+    from its exchange buffer (over NVLink) straight into the output's
+    columns, while the next block's GEMM runs.  No collective library call,
+    no staging copy, no reorder pass.  The current stream waits for the
+    communication stream at the end (the call captures into a CUDA graph).
+
+    Failure: as ``PeerExchange`` -- bounded waits, device error 7 and a mark
+    in the sync area; ``check()`` raises once the mark is seen and ``gemm``
+    then refuses; recovery is ``close()`` on every rank and a new exchange.
+    Unlike the decode exchange, the GEMMs do not read the mark, so a peer
+    slower than the wait limit could read a partly overwritten buffer of the
+    failed call: the limit must stay far above any call's duration."""
+
+    def __init__(self, group: Optional[dist.ProcessGroup] = None, max_rows: int = 4096, max_n_local: int = 14336):
+        if not dist.is_initialized():
+            raise RuntimeError("PrefillExchange needs an initialised process group")
+        if max_rows < 1 or max_n_local < 8 or max_n_local % 8:
+            raise ValueError("PrefillExchange: need max_rows >= 1 and max_n_local a positive multiple of 8")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _capi.MAX_PEERS:
+            raise ValueError(f"the peer exchange supports at most {_capi.MAX_PEERS} ranks, got {self.world}")
+        self.max_rows, self.max_n_local = max_rows, max_n_local
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        header = struct.pack("<qqqq", 2, self.world, max_rows, max_n_local)
+        self._xb = _SharedBuffer(2 * max_rows * max_n_local, group, self.rank, header)
+        try:
+            self._sync = _SharedBuffer(_capi.PX_SYNC_BYTES, group, self.rank, header)
+        except Exception:
+            self._xb.release()
+            raise
+        self._xb_elems = max_rows * max_n_local
+        self._xb_flat = _device_view(self._xb.local, (self._xb_elems,), torch.float16, self.device)
+        self._sync_words = _device_view(self._sync.local, (_capi.PX_SYNC_BYTES // 4,), torch.int32, self.device)
+        self._failed: Optional[str] = None
+
+    def calls_started(self) -> int:
+        """Exchange calls this rank has begun (synchronises)."""
+        return int(self._sync_words[0].item())
+
+    def check(self) -> None:
+        """Raise if a wait of an exchange call on this rank gave up
+        (synchronises); from then on ``gemm`` refuses further calls."""
+        if self._failed is None:
+            mark = int(self._sync_words[_capi.PX_SYNC_ABORT_WORD].item())
+            if mark != 0:
+                self._failed = f"a wait of prefill exchange call {mark} gave up (a peer's block did not arrive in time)"
+        if self._failed is not None:
+            raise RuntimeError(f"PrefillExchange failed: {self._failed}; close() it on every rank and set up a "
+                               "new one")
+
+    def supports(self, M: int, n_local: int) -> bool:
+        return 1 <= M and n_local % 8 == 0 and M * n_local <= self._xb_elems and n_local <= self.max_n_local
+
+    def gemm(self, x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
+             bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None, blocks=None) -> torch.Tensor:
+        """``out[M, world * n_local]``: every rank's slice of ``x2d @
+        (weight_int8 * scale[:, None]).T (+ bias)``, this rank's computed
+        here from its shard ``weight_int8 [n_local, K]``.  ``blocks``: the
+        row blocks ``[(row0, rows), ...]`` (default: the pipeline model's
+        choice, identical on every rank)."""
+        if self._xb is None:
+            raise RuntimeError("PrefillExchange is closed")
+        if self._failed is not None:
+            raise RuntimeError(f"PrefillExchange failed: {self._failed}; close() it on every rank and set up a "
+                               "new one")
+        M, K = x2d.shape
+        n_local = weight_int8.shape[0]
+        if not self.supports(M, n_local):
+            raise ValueError(f"prefill exchange sized for {self.max_rows} x {self.max_n_local} per rank "
+                             f"(n_local a multiple of 8), got {M} x {n_local}")
+        dev = x2d.device
+        if out is None:
+            out = torch.empty((M, self.world * n_local), dtype=torch.float16, device=dev)
+        if blocks is None:
+            from .sharded import prefill_row_blocks
+            blocks = prefill_row_blocks(M, n_local, K, self.world, _capi.device_sm_count(dev.index), "p2p")
+        if len(blocks) > _capi.PX_MAX_BLOCKS:
+            raise ValueError(f"at most {_capi.PX_MAX_BLOCKS} blocks per call")
+        xb = self._xb_flat[:M * n_local].view(M, n_local)
+        cur = torch.cuda.current_stream(dev)
+        comm = comm_stream(dev)
+        _capi.prefill_exchange_begin(self._sync.ptrs, self.rank, cur.cuda_stream)
+        for b, (r0, rows) in enumerate(blocks):
+            _capi.w8a16_gemm(x2d[r0:r0 + rows], weight_int8, scale, bias, out=xb[r0:r0 + rows])
+            done = torch.cuda.Event()
+            done.record(cur)
+            comm.wait_event(done)
+            _capi.prefill_exchange_block(self._xb.ptrs, n_local, self._sync.ptrs, self.rank, b, b == len(blocks) - 1,
+                                         r0, rows, n_local, out, comm.cuda_stream)
+        cur.wait_stream(comm)
+        return out
+
+    def close(self) -> None:
+        """Collective: wait for every rank's work, then unmap and free."""
+        if self._xb is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._xb.unmap()
+        self._sync.unmap()
+        dist.barrier(group=self.group)
+        self._xb_flat = None
+        self._sync_words = None
+        self._xb.release()
+        self._sync.release()
+        self._xb = None

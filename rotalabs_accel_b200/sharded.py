@@ -29,13 +29,14 @@ exactly the rows the full quantization would.
 
 from __future__ import annotations
 
+import functools
 from typing import Optional
 
 import torch
 import torch.distributed as dist
 
 from .gemm import int8_gemm
-from .peer import PeerExchange
+from .peer import PeerExchange, PrefillExchange, comm_stream
 from .quantization import quantize_weight_per_channel
 
 
@@ -80,11 +81,11 @@ def assemble_columns(staging: torch.Tensor, n_total: int, out: Optional[torch.Te
 
 # Block sizes of the overlapped prefill, from a two-stream pipeline model:
 # the local GEMM of a block takes whole waves of tiles (tcgen05 kernel, one
-# tile per SM at a time), and the all-gather plus reorder of a block runs
-# while the next block's GEMM does.  Figures measured on B200: about
-# 7.4 TFLOP/s per SM for 256-row tiles and 6.4 for 128-row tiles; the NCCL
-# all-gather delivers about 650 GB/s into each rank; the reorder moves about
-# 5 TB/s.
+# tile per SM at a time, blocks on one stream run one after the other), and
+# the all-gather plus reorder of a block runs while the next block's GEMM
+# does.  Figures measured on B200: about 7.4 TFLOP/s per SM for 256-row tiles
+# and 6.4 for 128-row tiles; the NCCL all-gather delivers about 650 GB/s into
+# each rank after ~15 us of start-up; the reorder moves about 5 TB/s.
 def _gemm_us(rows: int, n_local: int, K: int, sms: int) -> float:
     nt = -(-n_local // 128)
 
@@ -92,36 +93,76 @@ def _gemm_us(rows: int, n_local: int, K: int, sms: int) -> float:
         return -(-(nt * -(-rows // bm)) // sms)
 
     # the library's own choice of tile height (rla_capi.cu, make_plan)
-    bm = 256 if rows > 128 and waves(256) * 256 * 1.0 <= waves(128) * 128 * 1.16 else 128
-    rate = 7.4e12 if bm == 256 else 6.4e12
+    if rows > 128 and waves(256) * 256 * 1.0 <= waves(128) * 128 * 1.16:
+        bm, rate = 256, 7.4e12
+    elif rows > 64:
+        bm, rate = 128, 6.4e12
+    else:
+        bm, rate = 64, 4.0e12
     return waves(bm) * (2.0 * 128 * bm * K / rate) * 1e6
 
 
-def prefill_row_blocks(M: int, n_local: int, K: int = 8192, world: int = 2, sms: int = 148):
-    """``[(row0, rows), ...]`` covering ``[0, M)`` (blocks of equal size, a
-    multiple of 128 rows, but the last): of the splits into about 1, 2, 4 or
-    8 blocks, the one with the least modelled time; 1 block is the serial
-    GEMM -> all-gather -> reorder."""
+def _exchange_us(rows: int, n_local: int, world: int, kind: str = "nccl") -> float:
+    if kind == "p2p":
+        # pull exchange: each rank reads the peers' slices over NVLink at
+        # about 700 GB/s (its own slice is a local copy beside it)
+        return 6.0 + (world - 1) * rows * n_local * 2 / 700e9 * 1e6
+    ag = 15.0 + (world - 1) * rows * n_local * 2 / 650e9 * 1e6
+    reorder = 2.0 * rows * world * n_local * 2 / 5e12 * 1e6
+    return ag + reorder
+
+
+def _compositions(units: int, parts: int):
+    if parts == 1:
+        yield (units,)
+        return
+    for first in range(1, units - parts + 2):
+        for rest in _compositions(units - first, parts - 1):
+            yield (first,) + rest
+
+
+@functools.lru_cache(maxsize=256)
+def prefill_row_blocks(M: int, n_local: int, K: int = 8192, world: int = 2, sms: int = 148, exchange: str = "nccl"):
+    """``[(row0, rows), ...]`` covering ``[0, M)`` in order: 1 to 4 blocks of
+    rows, each a multiple of 128 rows but the last (which takes the ragged
+    tail, so no block is shorter than 128 rows unless M is), with the least
+    modelled time.  Blocks need not be equal: a GEMM whose tiles end in a partial wave
+    is cut where the waves are full (e.g. 13 + 3 row tiles of 256 rows for a
+    4096 x 14336 shard on 148 SMs), so the blocks cost no more GEMM waves than
+    the whole, and the short last block leaves little exchange exposed.  One
+    block is the serial GEMM -> all-gather -> reorder; more blocks are taken
+    only for a clear gain (3 %).  ``exchange``: "nccl" (all-gather, then
+    reorder) or "p2p" (``PrefillExchange``'s pull over NVLink)."""
+    units = max(1, M // 128)     # a ragged tail of rows joins the last block
+    gemm = {}
+    comm = {}
+
+    def rows_of(u0, u):
+        return M - u0 * 128 if u0 + u == units else u * 128
+
     best, best_t = None, None
-    for c in (1, 2, 4, 8):
-        rows = -(-M // c)
-        rows = -(-rows // 128) * 128
-        blocks, r0 = [], 0
-        while r0 < M:
-            blocks.append((r0, min(rows, M - r0)))
-            r0 += rows
-        t_gemm = t_comm = 0.0
-        for _, r in blocks:
-            t_gemm += _gemm_us(r, n_local, K, sms)
-            ag = 15.0 + (world - 1) * r * n_local * 2 / 650e9 * 1e6
-            reorder = 2.0 * r * world * n_local * 2 / 5e12 * 1e6
-            t_comm = max(t_gemm, t_comm) + ag + reorder
-        if best_t is None or t_comm < best_t * 0.97:   # more blocks only for a clear gain
-            best, best_t = blocks, t_comm
-    return best
-
-
-_comm_streams: dict = {}
+    for c in range(1, min(4, units) + 1):
+        c_best, c_t = None, None
+        for comp in _compositions(units, c):
+            t_gemm = t_done = 0.0
+            u0 = 0
+            for u in comp:
+                r = rows_of(u0, u)
+                if r not in gemm:
+                    gemm[r] = _gemm_us(r, n_local, K, sms)
+                    comm[r] = _exchange_us(r, n_local, world, exchange)
+                t_gemm += gemm[r]
+                t_done = max(t_gemm, t_done) + comm[r]
+                u0 += u
+            if c_t is None or t_done < c_t:
+                c_best, c_t = comp, t_done
+        if best_t is None or c_t < best_t * 0.97:
+            best, best_t = c_best, c_t
+    blocks, u0 = [], 0
+    for u in best:
+        blocks.append((u0 * 128, rows_of(u0, u)))
+        u0 += u
+    return blocks
 
 
 def prefill_overlapped(x2: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
@@ -143,9 +184,7 @@ def prefill_overlapped(x2: torch.Tensor, weight_int8: torch.Tensor, scale: torch
     if out is None:
         out = torch.empty((M, n_total), dtype=torch.float16, device=dev)
     cur = torch.cuda.current_stream(dev)
-    comm = _comm_streams.get(dev.index)
-    if comm is None:
-        comm = _comm_streams[dev.index] = torch.cuda.Stream(device=dev)
+    comm = comm_stream(dev)
     from . import _capi
     blocks = prefill_row_blocks(M, n_local, K, world, _capi.device_sm_count(dev.index))
     # every buffer is allocated here on the current stream and lives until
@@ -191,6 +230,8 @@ class ColumnParallelInt8Linear(torch.nn.Module):
         self._quantized = False
         self._exchange: Optional[PeerExchange] = None
         self._owns_exchange = False
+        self._prefill: Optional[PrefillExchange] = None
+        self._owns_prefill = False
 
     def _check_agreement(self) -> None:
         """Every rank must shard the same layer: compare (in, out, world) over
@@ -234,12 +275,14 @@ class ColumnParallelInt8Linear(torch.nn.Module):
             self.bias.data[:rows].copy_(bias[self.start:self.stop])
         self._quantized = True
 
-    def enable_peer_exchange(self, max_tokens: int = 32, exchange: Optional[PeerExchange] = None) -> None:
+    def enable_peer_exchange(self, max_tokens: int = 32, exchange: Optional[PeerExchange] = None,
+                             max_prefill_tokens: int = 0, prefill_exchange: Optional[PrefillExchange] = None) -> None:
         """Collective (every rank, module already on its GPU): use the fused
         peer-to-peer path for batches of up to ``max_tokens`` rows (at most
-        32).  ``exchange`` may be shared by several layers (it must be sized
-        for this layer's rows and columns per rank); by default the layer
-        makes its own."""
+        32), and, with ``max_prefill_tokens`` > 32 (or a ``prefill_exchange``),
+        the pull exchange for longer batches of up to that many rows.  Either
+        exchange may be shared by several layers (sized for their rows and
+        columns per rank); by default the layer makes its own."""
         if not 1 <= max_tokens <= 32:
             raise ValueError("max_tokens must be in [1, 32] (the decode kernels)")
         if not self.weight_int8.is_cuda:
@@ -251,13 +294,23 @@ class ColumnParallelInt8Linear(torch.nn.Module):
             raise ValueError("enable_peer_exchange: the shared exchange is too small for this layer")
         self._exchange = exchange
         self._max_tokens = max_tokens
+        if prefill_exchange is None and max_prefill_tokens > 32 and self.n_local % 8 == 0:
+            prefill_exchange = PrefillExchange(self.group, max_rows=max_prefill_tokens, max_n_local=self.n_local)
+            self._owns_prefill = True
+        elif prefill_exchange is not None and not prefill_exchange.supports(prefill_exchange.max_rows, self.n_local):
+            raise ValueError("enable_peer_exchange: the shared prefill exchange is too small for this layer")
+        self._prefill = prefill_exchange
 
     def close_peer_exchange(self) -> None:
-        """Collective: release the fused path's buffers (when the layer owns them)."""
+        """Collective: release the peer paths' buffers (those the layer owns)."""
         if self._exchange is not None and self._owns_exchange:
             self._exchange.close()
+        if self._prefill is not None and self._owns_prefill:
+            self._prefill.close()
         self._exchange = None
         self._owns_exchange = False
+        self._prefill = None
+        self._owns_prefill = False
 
     def _fused_ok(self, x2: torch.Tensor) -> bool:
         return (self._exchange is not None and x2.is_cuda and x2.dtype == torch.float16
@@ -276,13 +329,17 @@ class ColumnParallelInt8Linear(torch.nn.Module):
             if y.shape[1] != self.out_features:
                 y = y[:, :self.out_features]
             return y.reshape(*lead, self.out_features)
-        if (self.world > 1 and x2.is_cuda and M >= 1024 and x2.dtype == torch.float16 and x2.stride(1) == 1
-                and self.weight_int8.stride(1) == 1):
+        pull = (self._prefill is not None and M > 32 and self._prefill.supports(M, self.n_local))
+        if (self.world > 1 and x2.is_cuda and (M >= 1024 or pull) and x2.dtype == torch.float16
+                and x2.stride(1) == 1 and self.weight_int8.stride(1) == 1):
             b = self.bias
             if b is not None and b.dtype not in (torch.float16, torch.float32):
                 b = b.half()
-            y = prefill_overlapped(x2, self.weight_int8, self.scale, b, self.world * self.n_local, self.world,
-                                   group=self.group)
+            if pull:
+                y = self._prefill.gemm(x2, self.weight_int8, self.scale, b)
+            else:
+                y = prefill_overlapped(x2, self.weight_int8, self.scale, b, self.world * self.n_local, self.world,
+                                       group=self.group)
             if y.shape[1] != self.out_features:
                 y = y[:, :self.out_features]
             return y.reshape(*lead, self.out_features)

@@ -168,3 +168,66 @@ def test_exchange_refuses_calls_after_a_failed_wait():
     ex._sync[_capi.PEER_SYNC_ABORT_WORD] = 0  # the mark stays on the host side too
     with pytest.raises(RuntimeError, match="PeerExchange failed"):
         ex.check()
+
+
+def test_prefill_exchange_rejects_bad_arguments(lib):
+    """rla_prefill_exchange_begin / _block validate everything before any
+    launch (no device is touched by these calls)."""
+    fake = 1 << 20
+    syncs = _arr([fake, fake + 4096])
+    xbs = _arr([fake, fake + (1 << 24)])
+
+    def blk(**kw):
+        a = dict(xb=xbs, ld=128, sync=syncs, rank=0, world=2, block=0, last=1, row0=0, rows=256, nl=128, y=fake,
+                 ldy=256)
+        a.update(kw)
+        return lib.rla_prefill_exchange_block(a["xb"], a["ld"], a["sync"], a["rank"], a["world"], a["block"],
+                                              a["last"], a["row0"], a["rows"], a["nl"], a["y"], a["ldy"], None)
+
+    assert lib.rla_prefill_exchange_begin(syncs, 0, 0, None) == 1
+    assert lib.rla_prefill_exchange_begin(syncs, 2, 2, None) == 1
+    assert lib.rla_prefill_exchange_begin(None, 0, 2, None) == 1
+    assert lib.rla_prefill_exchange_begin(_arr([fake, fake + 64]), 0, 2, None) == 1   # sync not 128-byte aligned
+    assert blk(world=9) == 1
+    assert blk(rank=-1) == 1
+    assert blk(xb=None) == 1
+    assert blk(xb=_arr([fake, fake + 8])) == 1          # exchange buffer not 16-byte aligned
+    assert blk(sync=_arr([fake, 0])) == 1
+    assert blk(y=fake + 8) == 1
+    assert blk(block=16) == 1                           # at most RLA_PX_MAX_BLOCKS blocks
+    assert blk(block=-1) == 1
+    assert blk(nl=100, ld=100, ldy=200) == 1            # n_local not a multiple of 8
+    assert blk(ld=64) == 1                              # ld_xb < n_local
+    assert blk(ldy=255) == 1                            # ldy < world * n_local
+    assert blk(rows=-1) == 1
+    assert blk(rows=1 << 31) == 1                       # rows >= 2^31
+    assert b"2^31" in lib.rla_last_error()
+
+
+def test_prefill_exchange_refuses_calls_after_a_failed_wait():
+    """The pull exchange's host-side failure rule, as for the decode exchange:
+    a marked sync area makes check() raise and gemm() refuse.  The object is
+    assembled by hand around a CPU copy of the sync words."""
+    from rotalabs_accel_b200 import _capi
+    from rotalabs_accel_b200.peer import PrefillExchange
+    ex = PrefillExchange.__new__(PrefillExchange)
+    ex._xb = object()
+    ex._failed = None
+    ex.max_rows, ex.max_n_local, ex._xb_elems = 64, 128, 64 * 128
+    ex._sync_words = torch.zeros(_capi.PX_SYNC_BYTES // 4, dtype=torch.int32)
+    ex.check()
+    assert ex.supports(64, 128) and not ex.supports(65, 128) and not ex.supports(8, 100)
+    ex._sync_words[_capi.PX_SYNC_ABORT_WORD] = 3
+    with pytest.raises(RuntimeError, match="call 3 gave up"):
+        ex.check()
+    with pytest.raises(RuntimeError, match="set up a new one"):
+        ex.gemm(torch.zeros(64, 32, dtype=torch.float16), torch.zeros(128, 32, dtype=torch.int8),
+                torch.ones(128))
+
+
+def test_prefill_exchange_needs_a_process_group():
+    from rotalabs_accel_b200.peer import PrefillExchange
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised")
+    with pytest.raises(RuntimeError, match="process group"):
+        PrefillExchange()

@@ -11,10 +11,17 @@ One GPU:
     never sends anything makes the bounded wait give up (short limit), the
     kernel returns, the device error word reads 7 ("a peer's slice did not
     arrive") and the context stays usable.
+  * the prefill pull exchange (PrefillExchange) at world = 1: y equals the
+    plain GEMM of the same row blocks bit for bit, eagerly and under graph
+    replay; and a two-rank call whose second "rank" never marks its block
+    gives up after a short limit with device error 7, then 9 on the next
+    call, without a fault.
 Two or more GPUs (skipped otherwise): one process per GPU over NCCL, the
 column-parallel layer's fused path equals its NCCL path and the fp32
 reference within tolerance, call after call, for every decode kernel,
-with several layers sharing one exchange and under graph replay.
+with several layers sharing one exchange and under graph replay; the
+prefill pull exchange and the NCCL-overlapped prefill against the fp32
+reference, the pull also under graph replay with ragged blocks.
 """
 
 import datetime
@@ -185,6 +192,96 @@ def test_missing_peer_times_out_with_error_status(single_rank_group, kernel):
             _capi.peer_free(p)
 
 
+def _px_blocks(M):
+    """Uneven row blocks (the last ragged) for the pull-exchange tests."""
+    if M <= 256:
+        return [(0, M)]
+    a = (M // 3) // 128 * 128 or 128
+    return [(0, a), (a, 128), (a + 128, M - a - 128)] if M - a - 128 > 0 else [(0, a), (a, M - a)]
+
+
+@pytest.mark.parametrize("M,K,N", [(1024, 4096, 4096), (300, 1024, 1000), (517, 2048, 2048), (64, 512, 256)])
+def test_world1_prefill_pull_equals_plain(single_rank_group, M, K, N):
+    """A single-rank pull exchange: the GEMM of every row block goes through
+    the exchange buffer, the pull copies it into y; y equals the plain GEMM
+    of the same row blocks bit for bit, and the call number advances once
+    per call (eager and under CUDA-graph replay)."""
+    from rotalabs_accel_b200 import _capi
+    from rotalabs_accel_b200.peer import PrefillExchange
+    ex = PrefillExchange(max_rows=1024, max_n_local=4096)
+    try:
+        x, q, s, b = _problem(M, N, K, 400 + M, bias=True)
+        blocks = _px_blocks(M)
+        ref = torch.cat([_capi.w8a16_gemm(x[r0:r0 + r], q, s, b) for r0, r in blocks])
+        y = ex.gemm(x, q, s, b, blocks=blocks)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)
+        assert ex.calls_started() == 1
+        out = torch.zeros_like(ref)
+        stream = torch.cuda.Stream()
+        with torch.cuda.stream(stream):
+            ex.gemm(x, q, s, b, out=out, blocks=blocks)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            ex.gemm(x, q, s, b, out=out, blocks=blocks)
+        out.zero_()
+        for _ in range(5):
+            g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        assert ex.calls_started() == 7
+        assert _capi.device_error() == 0
+        ex.check()
+        del g
+    finally:
+        ex.close()
+
+
+def test_prefill_pull_missing_peer_times_out_with_error_status(single_rank_group):
+    """A two-rank pull whose second "rank" is a pair of local buffers that no
+    kernel ever marks: the wait for its block runs out (50 ms), the kernel
+    returns, the error word reads 7, the sync area keeps the mark, the next
+    call records 9 and returns at once, and the context stays usable."""
+    from rotalabs_accel_b200 import _capi
+    bufs = []
+    try:
+        _capi.set_peer_wait_limit(0.05)
+        M, N, K = 256, 1024, 2048
+        x, q, s, _ = _problem(M, N, K, 500)
+        bufs = [_capi.peer_alloc(M * N * 2) for _ in range(2)] + [_capi.peer_alloc(_capi.PX_SYNC_BYTES)
+                                                                    for _ in range(2)]
+        xbs, syncs = bufs[:2], bufs[2:]
+        from rotalabs_accel_b200.peer import _device_view
+        xb = _device_view(xbs[0], (M, N), torch.float16, torch.device("cuda"))
+        words = _device_view(syncs[0], (_capi.PX_SYNC_BYTES // 4,), torch.int32, torch.device("cuda"))
+        out = torch.zeros(M, 2 * N, dtype=torch.float16, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        assert _capi.device_error() == 0
+        _capi.prefill_exchange_begin(syncs, 0, stream)
+        _capi.w8a16_gemm(x, q, s, None, out=xb)
+        _capi.prefill_exchange_block(xbs, N, syncs, 0, 0, True, 0, M, N, out, stream)
+        torch.cuda.synchronize()
+        assert _capi.device_error() == 7
+        assert int(words[_capi.PX_SYNC_ABORT_WORD]) == 1
+        # this rank's own slice arrived; the missing peer's columns did not
+        assert torch.equal(out[:, :N], _capi.w8a16_gemm(x, q, s, None))
+        assert int(out[:, N:].abs().max()) == 0
+        _capi.prefill_exchange_begin(syncs, 0, stream)
+        _capi.prefill_exchange_block(xbs, N, syncs, 0, 0, True, 0, M, N, out, stream)
+        torch.cuda.synchronize()
+        assert _capi.device_error() == 9
+        assert int(words[0]) == 1          # the poisoned call did not advance the call number
+        ref = _capi.w8a16_gemm(x, q, s, None)
+        torch.cuda.synchronize()
+        assert ref.abs().max() > 0 and _capi.device_error() == 0
+    finally:
+        _capi.set_peer_wait_limit(1.0)
+        torch.cuda.synchronize()
+        for p in bufs:
+            _capi.peer_free(p)
+
+
 # --------------------------------------------------------------------------
 # two or more GPUs
 # --------------------------------------------------------------------------
@@ -286,6 +383,47 @@ def _worker_multi(rank, world, port, q):
                 report.append(("prefill overlapped", M, K, N, err))
             del m, wq, s, x, y, ref
             torch.cuda.empty_cache()
+        # The pull exchange (PrefillExchange): every rank's assembled output
+        # against the fp32 reference, eagerly and under CUDA-graph replay, with
+        # the model's row blocks and with ragged ones.
+        from rotalabs_accel_b200.peer import PrefillExchange
+        pex = PrefillExchange(max_rows=2048, max_n_local=-(-28672 // world))
+        for (M, K, N) in [(1024, 8192, 28672), (2048, 28672, 8192), (333, 4096, 4096)]:
+            g = torch.Generator(device=dev).manual_seed(110 + K + M)
+            W = torch.randn(N, K, generator=g, device=dev) * 0.02
+            m = ColumnParallelInt8Linear(K, N).to(dev)
+            m.quantize_weights(W)
+            m.enable_peer_exchange(max_tokens=16, exchange=ex, prefill_exchange=pex)
+            wq, s = quantize_weight_per_channel(W)
+            del W
+            x = torch.randn(M, K, generator=g, device=dev).half()
+            ref = x.float() @ (wq.float() * s.float()[:, None]).t()
+            tol = 1e-2 * max(1.0, float(ref.abs().max()))
+            y = m(x)
+            torch.cuda.synchronize()
+            if float((y.float() - ref).abs().max()) > tol:
+                ok = False
+                report.append(("prefill pull", M, K, N, float((y.float() - ref).abs().max())))
+            out = torch.zeros(M, N, dtype=torch.float16, device=dev)
+            ragged = [(0, 128), (128, M - 128)] if M > 128 else [(0, M)]
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                pex.gemm(x, m.weight_int8, m.scale, None, out=out, blocks=ragged)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                pex.gemm(x, m.weight_int8, m.scale, None, out=out, blocks=ragged)
+            out.zero_()
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            if float((out.float() - ref).abs().max()) > tol:
+                ok = False
+                report.append(("prefill pull graph", M, K, N, float((out.float() - ref).abs().max())))
+            del graph, m, wq, s, x, y, ref, out
+            torch.cuda.empty_cache()
+        pex.check()
+        pex.close()
         # graph replay of several layers sharing the exchange
         layers = []
         for i, (M, K, N) in enumerate([(1, 4096, 4096), (8, 4096, 11008), (16, 4096, 14336)]):
