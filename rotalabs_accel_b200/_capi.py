@@ -51,7 +51,8 @@ PX_SYNC_ABORT_WORD = 1
 
 _lib = None
 _fast = None
-_torch_op = None
+_torch_op = None          # torch.ops.rla.w8a16_gemm.default (through the dispatcher)
+_torch_op_direct = None   # the same CUDA kernel function, called without the dispatcher
 _lib_lock = threading.Lock()
 
 
@@ -134,9 +135,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                 pass
             if os.path.exists(TORCH_OP_PATH):
                 try:
-                    torch.ops.load_library(TORCH_OP_PATH)
+                    # importing the extension module loads the library, whose
+                    # static registration defines torch.ops.rla.w8a16_gemm
+                    from . import _rla_torch_ops
+                    globals()["_torch_op_direct"] = _rla_torch_ops.w8a16_gemm
                     globals()["_torch_op"] = torch.ops.rla.w8a16_gemm.default
-                except (OSError, RuntimeError):
+                except (ImportError, OSError, RuntimeError, AttributeError):
                     pass
         _lib = lib
         return lib
@@ -200,8 +204,8 @@ def w8a16_gemm(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor
     ``[N, K]`` with unit inner stride; ``scale`` ``[N]`` fp32/fp16
     contiguous; ``bias`` ``[N]`` fp16/fp32 or None."""
     lib = _lib if _lib is not None else load_library()
-    if out is None and _torch_op is not None:
-        return _torch_op(x2d, weight_int8, scale, bias)
+    if out is None and _torch_op_direct is not None:
+        return _torch_op_direct(x2d, weight_int8, scale, bias)
     fast = _fast
     M, K = x2d.shape
     N = weight_int8.shape[0]

@@ -13,8 +13,10 @@ hot entry points, with the host C compiler into ``_rla_fast<EXT_SUFFIX>``
 next to the library, linked to it by soname with an ``$ORIGIN`` rpath; and
 ``csrc/rla_torch_op.cpp``, the ``torch.library`` registration of
 ``rla::w8a16_gemm`` over the same C ABI, against the installed torch's
-headers and libraries into ``_rla_torch_ops.so`` (loaded with
-``torch.ops.load_library``).
+headers and libraries into ``_rla_torch_ops.so``, which is also a Python
+extension module: importing it registers the op and gives its CUDA kernel
+function as ``_rla_torch_ops.w8a16_gemm`` (called without the dispatcher on
+the per-token path).
 """
 
 from __future__ import annotations
@@ -84,9 +86,11 @@ def build_torch_op(verbose: bool = False) -> str:
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     tmp = TORCH_OP_PATH + ".tmp"
     cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_EXTENSION_NAME=_rla_torch_ops", "-DTORCH_API_INCLUDE_EXTENSION_H",
            *[f"-I{p}" for p in cpp_extension.include_paths()], f"-I{cuda_inc}",
+           "-I" + sysconfig.get_paths()["include"],
            os.path.join(CSRC, "rla_torch_op.cpp"), "-L" + HERE, "-l:" + LIB_NAME, f"-L{tlib}",
-           "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch",
+           "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch", "-ltorch_python",
            "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tlib}", "-o", tmp]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)

@@ -18,9 +18,16 @@
 //
 // The Meta kernel gives the output's shape and dtype without computing, so
 // the op traces under FakeTensor / torch.compile as an opaque call.
+//
+// The same file is also a Python extension module (_rla_torch_ops) whose
+// w8a16_gemm calls the CUDA kernel function directly: the per-token hot path
+// (Int8Linear.forward) takes it to skip the dispatcher's schema parsing and
+// dispatch, a few microseconds of host time per call.  Same checks, same
+// launch, same result as the op.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
 #include <torch/library.h>
 
 #include <map>
@@ -102,6 +109,12 @@ at::Tensor w8a16_gemm_meta(const at::Tensor& x, const at::Tensor& w, const at::T
 }
 
 }  // namespace
+
+PYBIND11_MODULE(_rla_torch_ops, m) {
+  m.def("w8a16_gemm", &w8a16_gemm_cuda, "rla::w8a16_gemm's CUDA kernel function, called without the dispatcher",
+        pybind11::arg("x"), pybind11::arg("weight_int8"), pybind11::arg("scale"),
+        pybind11::arg("bias") = pybind11::none());
+}
 
 TORCH_LIBRARY(rla, m) {
   m.def("w8a16_gemm(Tensor x, Tensor weight_int8, Tensor scale, Tensor? bias=None) -> Tensor");

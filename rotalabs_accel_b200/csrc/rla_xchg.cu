@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(32) px_begin_kernel(PxArgs a) {
 
 // Grid: world * ctas_per_src CTAs; CTA b copies from source rank
 // b / ctas_per_src.
+template <int UNR>
 __global__ void __launch_bounds__(px::kPullThreads) px_pull_kernel(PxArgs a) {
   unsigned int* sync = a.sync[a.rank];
   __shared__ unsigned int s_c;
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(px::kPullThreads) px_pull_kernel(PxArgs a) {
     __syncthreads();
   }
   if (s_ok) {
-    // One warp per row of the source's slice: 16-byte loads, four in flight
+    // One warp per row of the source's slice: 16-byte loads, UNR in flight
     // per lane, consecutive lanes on consecutive 16-byte units (no index
     // division, a few instructions per unit, so the copy leaves the SM's
     // issue slots to the GEMM running beside it).
@@ -171,13 +172,12 @@ __global__ void __launch_bounds__(px::kPullThreads) px_pull_kernel(PxArgs a) {
       const uint4* __restrict__ from = from0 + static_cast<int64_t>(r) * a.ld_xb16;
       uint4* __restrict__ to = to0 + static_cast<int64_t>(r) * a.ldy16;
       int ch = lane;
-      for (; ch + 96 < chunks; ch += 128) {
-        const uint4 v0 = px_ld_cg(from + ch), v1 = px_ld_cg(from + ch + 32);
-        const uint4 v2 = px_ld_cg(from + ch + 64), v3 = px_ld_cg(from + ch + 96);
-        to[ch] = v0;
-        to[ch + 32] = v1;
-        to[ch + 64] = v2;
-        to[ch + 96] = v3;
+      for (; ch + 32 * (UNR - 1) < chunks; ch += 32 * UNR) {
+        uint4 v[UNR];
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) v[u] = px_ld_cg(from + ch + 32 * u);
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) to[ch + 32 * u] = v[u];
       }
       for (; ch < chunks; ch += 32) to[ch] = px_ld_cg(from + ch);
     }
@@ -210,6 +210,7 @@ namespace rla {
 // split would keep the GEMM's CTAs (about 166 KB of shared memory each) off
 // that SM until every pull CTA there has finished.  Asking for the largest
 // shared-memory split keeps the SMs ready for the GEMM.  Once per device.
+template <int UNR>
 static cudaError_t px_prepare_pull_kernel() {
   static std::atomic<unsigned long long> done_mask{0};
   int d = 0;
@@ -217,10 +218,19 @@ static cudaError_t px_prepare_pull_kernel() {
   if (e != cudaSuccess) return e;
   const unsigned long long bit = d >= 0 && d < 64 ? (1ull << d) : 0ull;
   if (bit && (done_mask.load(std::memory_order_relaxed) & bit)) return cudaSuccess;
-  e = cudaFuncSetAttribute(px_pull_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+  e = cudaFuncSetAttribute(px_pull_kernel<UNR>, cudaFuncAttributePreferredSharedMemoryCarveout,
                            cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess && bit) done_mask.fetch_or(bit, std::memory_order_relaxed);
   return e;
+}
+
+template <int UNR>
+static cudaError_t px_launch_pull(const PxArgs& a, cudaStream_t stream) {
+  const cudaError_t prep = px_prepare_pull_kernel<UNR>();
+  if (prep != cudaSuccess) return prep;
+  rla_clear_stale_launch_error();
+  px_pull_kernel<UNR><<<a.world * a.ctas_per_src, px::kPullThreads, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 static int px_fill_common(PxArgs& a, void* const* sync_peers, int rank, int world, const char* fn) {
@@ -314,14 +324,15 @@ int rla_prefill_exchange_block(const void* const* xb_peers, int64_t ld_xb, void*
   const int warps = px::kPullThreads / 32;
   const int64_t want = (device_sm_count() + world - 1) / world;
   a.ctas_per_src = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, (rows + warps - 1) / warps)));
-  const cudaError_t prep = px_prepare_pull_kernel();
-  if (prep != cudaSuccess) {
-    set_error("%s: %s", fn, cudaGetErrorString(prep));
-    return RLA_ERR_CUDA;
-  }
-  rla_clear_stale_launch_error();
-  px_pull_kernel<<<world * a.ctas_per_src, px::kPullThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  const cudaError_t e = cudaGetLastError();
+  int unroll = 4;
+#ifdef RLA_EXPERIMENTS
+  unroll = exp_int("RLA_PX_UNROLL", unroll);
+  if (const int c = exp_int("RLA_PX_CTAS", 0); c > 0)
+    a.ctas_per_src = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((c + world - 1) / world,
+                                                                            (rows + warps - 1) / warps)));
+#endif
+  const cudaError_t e = unroll == 8 ? px_launch_pull<8>(a, static_cast<cudaStream_t>(stream))
+                                    : px_launch_pull<4>(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     set_error("%s: launch failed: %s", fn, cudaGetErrorString(e));
     return RLA_ERR_CUDA;

@@ -80,7 +80,7 @@ def int8_gemm(x: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
     if x.is_cuda and weight_int8.is_cuda and scale.is_cuda:
         # (a 2-D fp16 x with unit inner stride, the per-token case, is used as is)
         plain = x.dim() == 2 and x.dtype == torch.float16 and (x.shape[0] == 0 or x.stride(1) == 1)
-        op = _capi._torch_op
+        op = _capi._torch_op_direct
         if (plain and op is not None and weight_int8.stride(1) == 1 and scale.is_contiguous()
                 and (bias is None or (bias.dtype in (torch.float16, torch.float32) and bias.is_contiguous()))):
             return op(x, weight_int8, scale, bias)
@@ -183,10 +183,11 @@ class Int8Linear(torch.nn.Module):
         # costs host time on every decode call)
         b = self._buffers
         w, s, bias = b["weight_int8"], b["scale"], self._parameters["bias"]
-        op = _capi._torch_op
-        # Per-token fast path straight to the library's op: a 2-D fp16 CUDA x
-        # of this layer's width with unit inner stride, contiguous buffers.
-        # Anything else takes int8_gemm's checks and conversions.
+        op = _capi._torch_op_direct
+        # Per-token fast path straight to the library's op (its CUDA kernel
+        # function, without the dispatcher): a 2-D fp16 CUDA x of this
+        # layer's width with unit inner stride, contiguous buffers.  Anything
+        # else takes int8_gemm's checks and conversions.
         if (op is not None and x.is_cuda and x.dim() == 2 and x.dtype == torch.float16
                 and x.shape[1] == self.in_features and x.stride(1) == 1 and w.is_cuda and w.is_contiguous()
                 and s.is_contiguous() and (bias is None or (bias.dtype == torch.float16 and bias.is_contiguous()))):

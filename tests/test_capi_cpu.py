@@ -198,6 +198,12 @@ def test_torch_library_op_registered():
     assert y.shape == (5, 40) and y.dtype == torch.float16 and y.device.type == "meta"
     y = torch.ops.rla.w8a16_gemm(x, w, s.half(), torch.empty(40, dtype=torch.float16, **meta))
     assert y.shape == (5, 40)
+    # the same CUDA kernel function, exported for calls without the dispatcher
+    # (the per-token path); its checks run before any device work
+    assert _capi._torch_op_direct is not None
+    import pytest
+    with pytest.raises(RuntimeError, match="Weight must be INT8"):
+        _capi._torch_op_direct(torch.empty(5, 96, dtype=torch.float16), torch.empty(40, 96), torch.empty(40))
     with pytest.raises(RuntimeError, match="Weight must be INT8"):
         torch.ops.rla.w8a16_gemm(x, w.to(torch.float16), s)
     with pytest.raises(RuntimeError, match="Scale shape mismatch"):
