@@ -259,14 +259,17 @@ static Plan make_plan_uncached(int64_t M, int64_t N, int64_t K, bool aligned, bo
     p.kernel = RLA_KERNEL_TCGEN05;
     const int64_t ntiles = (N + 127) / 128;
     // Tile height by whole waves of tiles (one CTA per SM): 256-row tiles
-    // unless 128-row tiles finish in less time; a 128-row tile does half the
-    // work of a 256-row one at about 16 % less throughput per FLOP (B200:
-    // ~7.4 vs ~6.4 TFLOP/s per SM).
+    // unless 128-row tiles finish in less time.  A 128-row tile does half the
+    // work of a 256-row one but takes 0.85-1.15 of its time (B200, measured
+    // over the Llama-70B shards at M = 512-4096: e.g. 28672 -> 1024 one wave
+    // of 128-row tiles 187 us, of 256-row tiles 207 us; 8192 -> 14336 at
+    // M = 768 five waves of 128-row tiles 282 us, while M = 1024 in four
+    // waves of 256-row tiles took 247 us), so 128 pays only with fewer waves.
     auto wave_cost = [&](int64_t bm, double rel) {
       const int64_t tiles = ntiles * ((M + bm - 1) / bm);
       return static_cast<double>((tiles + sms - 1) / sms) * static_cast<double>(bm) * rel;
     };
-    if (M > 128 && wave_cost(256, 1.0) <= wave_cost(128, 1.16)) {
+    if (M > 128 && wave_cost(256, 1.0) <= wave_cost(128, 1.9)) {
       p.bm = 256; p.stages = 4;
     } else if (M > 64) {
       p.bm = 128; p.stages = 6;

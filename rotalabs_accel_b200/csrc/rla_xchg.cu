@@ -15,9 +15,9 @@
 //        (ready[r][block] = c; a release store at system scope, ordered after
 //        the GEMM's stores by the stream and the kernel boundary);
 //      - it waits (bounded) for ready[src][block] >= c of the source rank it
-//        copies from, then reads that rank's rows of the block from xb[src]
-//        over NVLink (16-byte loads that bypass L1) and stores them into
-//        y[rows, src * n_local : (src + 1) * n_local];
+//        copies from, then moves that rank's rows of the block from xb[src]
+//        (over NVLink for a peer) into y[rows, src * n_local : (src + 1) *
+//        n_local] with bulk copies through shared memory;
 //      - on the call's last block, the last CTA to finish tells every peer
 //        that r's reads of call c are over (done[r] = c in the peer's sync
 //        area).
@@ -32,8 +32,8 @@
 //
 // No cross-GPU deadlock: a pull waits only for peers' GEMMs of the same call
 // and block, which wait on nothing but their own begin, which waits only on
-// reads of the previous call.  Pull CTAs need no shared memory and few
-// registers, so they fit beside the tcgen05 GEMM's CTAs on the same SM.
+// reads of the previous call.  A pull CTA is one warp with 48 KB of shared
+// memory, so it fits beside a tcgen05 GEMM CTA on the same SM.
 //
 // Every wait is bounded by the limit of rla_set_peer_wait_limit.  A wait that
 // gives up records device error 7 and marks the sync area aborted (the call
@@ -56,7 +56,9 @@ constexpr int kDone = 16;     // + src: last call whose reads of this rank's buf
 constexpr int kReady = 32;    // + src * kMaxBlocks + block: call number of src's block
 constexpr int kMaxBlocks = RLA_PX_MAX_BLOCKS;
 static_assert(kReady + kMaxPeers * kMaxBlocks <= RLA_PX_SYNC_BYTES / 4, "prefill exchange sync area layout");
-constexpr int kPullThreads = 256;
+constexpr int kSlots = 3;             // pull ring: slots of shared memory per CTA
+constexpr int kSlotBytes = 16384;
+constexpr int kPullSmem = kSlots * kSlotBytes;
 }  // namespace px
 
 struct PxArgs {
@@ -80,14 +82,6 @@ RLA_DEVFN unsigned int px_ld_acquire_sys(const unsigned int* p) {
 }
 RLA_DEVFN void px_st_release_sys(unsigned int* p, unsigned int v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-RLA_DEVFN uint4 px_ld_cg(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
 }
 // a >= b for call numbers that may wrap
 RLA_DEVFN bool px_reached(unsigned int a, unsigned int b) { return static_cast<int>(a - b) >= 0; }
@@ -132,63 +126,148 @@ __global__ void __launch_bounds__(32) px_begin_kernel(PxArgs a) {
   if (src < a.world && src != a.rank) (void)px_wait(sync + px::kDone + src, c - 1u, sync, a.wait_ns);
 }
 
-// Grid: world * ctas_per_src CTAs; CTA b copies from source rank
-// b / ctas_per_src.
-template <int UNR>
-__global__ void __launch_bounds__(px::kPullThreads) px_pull_kernel(PxArgs a) {
-  unsigned int* sync = a.sync[a.rank];
-  __shared__ unsigned int s_c;
-  __shared__ int s_ok;
-  const int src = blockIdx.x / a.ctas_per_src;
-  const int part = blockIdx.x % a.ctas_per_src;
-  if (threadIdx.x == 0) {
-    const unsigned int c = rla_ld_relaxed_gpu_u32(sync + px::kSeq);
-    const unsigned int aborted = rla_ld_relaxed_gpu_u32(sync + px::kAbort);
-    s_c = c;
-    s_ok = aborted == 0u;
-    if (aborted != 0u && aborted != c) rla_record_error(RLA_DEVERR_PEER_POISONED);
-  }
-  __syncthreads();
-  const unsigned int c = s_c;
-  if (s_ok) {
-    // announce this rank's block to every rank (idempotent across CTAs)
-    if (threadIdx.x < a.world)
-      px_st_release_sys(a.sync[threadIdx.x] + px::kReady + a.rank * px::kMaxBlocks + a.block, c);
-    if (threadIdx.x == 0)
-      s_ok = px_wait(sync + px::kReady + src * px::kMaxBlocks + a.block, c, sync, a.wait_ns) ? 1 : 0;
-    __syncthreads();
-  }
-  if (s_ok) {
-    // One warp per row of the source's slice: 16-byte loads, UNR in flight
-    // per lane, consecutive lanes on consecutive 16-byte units (no index
-    // division, a few instructions per unit, so the copy leaves the SM's
-    // issue slots to the GEMM running beside it).
-    constexpr int kWarps = px::kPullThreads / 32;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int chunks = a.chunks;
-    const uint4* __restrict__ from0 = a.xb[src] + a.row0 * a.ld_xb16;
-    uint4* __restrict__ to0 = a.y + a.row0 * a.ldy16 + static_cast<int64_t>(src) * chunks;
-    for (int r = part * kWarps + warp; r < a.rows; r += a.ctas_per_src * kWarps) {
-      const uint4* __restrict__ from = from0 + static_cast<int64_t>(r) * a.ld_xb16;
-      uint4* __restrict__ to = to0 + static_cast<int64_t>(r) * a.ldy16;
-      int ch = lane;
-      for (; ch + 32 * (UNR - 1) < chunks; ch += 32 * UNR) {
-        uint4 v[UNR];
-#pragma unroll
-        for (int u = 0; u < UNR; ++u) v[u] = px_ld_cg(from + ch + 32 * u);
-#pragma unroll
-        for (int u = 0; u < UNR; ++u) to[ch + 32 * u] = v[u];
-      }
-      for (; ch < chunks; ch += 32) to[ch] = px_ld_cg(from + ch);
+// ---------------------------------------------------------------------------
+// The pull moves bytes with the SM's bulk-copy engine (TMA, untiled): one warp
+// per CTA, its lane 0 streams the source's rows through a ring of
+// shared-memory slots -- a bulk load from the source's exchange buffer (over
+// NVLink for a peer) completing on an mbarrier, then a bulk store into y.
+// Few instructions per byte and no load/store-unit traffic, so the pull
+// costs the GEMM running beside it on the same SMs as little as it can.
+// Plain loads, no multicast.  A CTA's rows are one contiguous range; a slot
+// holds whole rows when they fit (one load for several rows, one store per
+// row), else one piece of a row.
+// ---------------------------------------------------------------------------
+RLA_DEVFN void px_bulk_load(void* smem, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  rla_mbar_arrive_expect_tx(bar, bytes);
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   rla_smem_u32(smem)),
+               "l"(gsrc), "r"(bytes), "r"(rla_smem_u32(bar))
+               : "memory");
+}
+RLA_DEVFN void px_bulk_store(void* gdst, const void* smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(rla_smem_u32(smem)),
+               "r"(bytes)
+               : "memory");
+}
+RLA_DEVFN void px_bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+RLA_DEVFN void px_bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+RLA_DEVFN void px_bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// After a failed wait: wait (bounded again) for a bulk load this CTA issued,
+// so that no copy into its shared memory is in flight when it exits.
+RLA_DEVFN void px_drain_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = rla_globaltimer();
+  while (!rla_mbar_try_wait_sleep(bar, parity, 1000u))
+    if (rla_globaltimer() - t0 > limit_ns) return;
+}
+
+// Piece walker over rows [r, re) of one CTA: a piece is `nr` whole rows
+// (rows_per_slot of them at most) or bytes [off, off + len) of one row.
+struct PxPiece {
+  int r, re, nr;
+  uint32_t off, len;
+  uint32_t rowbytes;
+  uint32_t slot_bytes;
+  int rows_per_slot;  // 0: rows larger than a slot
+  RLA_DEVFN bool valid() const { return r < re; }
+  RLA_DEVFN void settle() {
+    if (rows_per_slot > 0) {
+      nr = min(rows_per_slot, re - r);
+      off = 0;
+      len = static_cast<uint32_t>(nr) * rowbytes;
+    } else {
+      nr = 1;
+      len = min(slot_bytes, rowbytes - off);
     }
   }
+  RLA_DEVFN void next() {
+    if (rows_per_slot > 0) {
+      r += nr;
+    } else {
+      off += len;
+      if (off >= rowbytes) {
+        off = 0;
+        ++r;
+      }
+    }
+    settle();
+  }
+};
+
+__global__ void __launch_bounds__(32) px_pull_kernel(PxArgs a) {
+  extern __shared__ __align__(128) unsigned char px_ring[];
+  __shared__ __align__(8) uint64_t bars[px::kSlots];
+  __shared__ int s_abort;
+  unsigned int* sync = a.sync[a.rank];
+  const int src = blockIdx.x / a.ctas_per_src;
+  const int part = blockIdx.x % a.ctas_per_src;
+  const int lane = threadIdx.x;
+  unsigned int c = 0;
+  bool ok = false;
+  if (lane == 0) {
+    c = rla_ld_relaxed_gpu_u32(sync + px::kSeq);
+    const unsigned int aborted = rla_ld_relaxed_gpu_u32(sync + px::kAbort);
+    ok = aborted == 0u;
+    if (aborted != 0u && aborted != c) rla_record_error(RLA_DEVERR_PEER_POISONED);
+  }
+  c = __shfl_sync(0xffffffffu, c, 0);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (ok && lane < a.world) px_st_release_sys(a.sync[lane] + px::kReady + a.rank * px::kMaxBlocks + a.block, c);
+  if (ok && lane == 0) {
+    ok = px_wait(sync + px::kReady + src * px::kMaxBlocks + a.block, c, sync, a.wait_ns);
+    s_abort = 0;
+    for (int i = 0; i < px::kSlots; ++i) rla_mbar_init(&bars[i], 1);
+    rla_fence_barrier_init();
+    // the source's rows were written by generic stores (its GEMM) and are
+    // read here by the bulk-copy (async) proxy
+    asm volatile("fence.proxy.async;" ::: "memory");
+  }
+  if (ok && lane == 0) {
+    const int per = (a.rows + a.ctas_per_src - 1) / a.ctas_per_src;
+    const int rb = min(a.rows, part * per), re = min(a.rows, rb + per);
+    const uint32_t rowbytes = static_cast<uint32_t>(a.chunks) * 16u;
+    const bool packed = a.ld_xb16 == a.chunks && rowbytes <= static_cast<uint32_t>(px::kSlotBytes);
+    const int rps = packed ? static_cast<int>(px::kSlotBytes / rowbytes) : 0;
+    const char* from = reinterpret_cast<const char*>(a.xb[src] + a.row0 * a.ld_xb16);
+    char* to = reinterpret_cast<char*>(a.y + a.row0 * a.ldy16 + static_cast<int64_t>(src) * a.chunks);
+    const int64_t ld_from = a.ld_xb16 * 16, ld_to = a.ldy16 * 16;
+    PxPiece li{rb, re, 0, 0u, 0u, rowbytes, static_cast<uint32_t>(px::kSlotBytes), rps};
+    li.settle();
+    PxPiece si = li;
+    int issued = 0, done = 0;
+    while (issued < px::kSlots && li.valid()) {
+      px_bulk_load(px_ring + issued * px::kSlotBytes, from + li.r * ld_from + li.off, li.len, &bars[issued]);
+      li.next();
+      ++issued;
+    }
+    bool good = true;
+    while (done < issued) {
+      const int slot = done % px::kSlots;
+      const uint32_t parity = static_cast<uint32_t>(done / px::kSlots) & 1u;
+      if (good && !rla_mbar_wait(&bars[slot], parity, RLA_DEVERR_TIMEOUT_PEER_DATA, &s_abort)) good = false;
+      if (!good) px_drain_wait(&bars[slot], parity, a.wait_ns);  // a load in flight must land before exit
+      if (good) {
+        const unsigned char* sm = px_ring + slot * px::kSlotBytes;
+        for (int i = 0; i < si.nr; ++i)
+          px_bulk_store(to + (si.r + i) * ld_to + si.off, sm + i * si.rowbytes, si.nr > 1 ? si.rowbytes : si.len);
+        px_bulk_commit();
+        si.next();
+      }
+      ++done;
+      if (good && li.valid()) {
+        px_bulk_wait_read_all();  // the slot's data has left for y: reuse it
+        px_bulk_load(px_ring + slot * px::kSlotBytes, from + li.r * ld_from + li.off, li.len, &bars[slot]);
+        li.next();
+        ++issued;
+      }
+    }
+    px_bulk_wait_all();
+    asm volatile("fence.proxy.async;" ::: "memory");
+    if (!good) atomicCAS(sync + px::kAbort, 0u, c);
+  }
   if (a.last) {
-    // The last CTA of the call's last pull tells every peer that this rank's
-    // reads of call c are over (the earlier blocks' pulls completed before
-    // this launch started).  Aborted calls send nothing: the peers' begin
-    // then gives up too.
-    __syncthreads();
-    if (threadIdx.x == 0) {
+    __syncwarp();
+    if (lane == 0) {
       const unsigned int old = rla_arrive_acq_rel_gpu(sync + px::kTicket);
       if (old + 1u == gridDim.x && rla_ld_relaxed_gpu_u32(sync + px::kAbort) == 0u) {
         for (int d = 0; d < a.world; ++d)
@@ -204,32 +283,30 @@ __global__ void __launch_bounds__(px::kPullThreads) px_pull_kernel(PxArgs a) {
 // Host side.
 // ---------------------------------------------------------------------------
 namespace rla {
-// The pull kernel runs beside the tcgen05 GEMM on the same SMs.  An SM's
-// split between L1 and shared memory changes only when the SM is idle, so a
-// pull CTA that lands on an idle SM with the default (small shared memory)
-// split would keep the GEMM's CTAs (about 166 KB of shared memory each) off
-// that SM until every pull CTA there has finished.  Asking for the largest
-// shared-memory split keeps the SMs ready for the GEMM.  Once per device.
-template <int UNR>
-static cudaError_t px_prepare_pull_kernel() {
+// The pull kernel runs beside the tcgen05 GEMM on the same SMs (48 KB of
+// shared memory next to the GEMM's ~166 KB).  An SM's split between L1 and
+// shared memory changes only when the SM is idle, so the kernel asks for the
+// largest shared-memory split: a pull CTA that lands on an idle SM then
+// leaves room for a GEMM CTA.  Attributes set once per device.
+static cudaError_t px_launch_pull(PxArgs a, int ctas_total, cudaStream_t stream) {
   static std::atomic<unsigned long long> done_mask{0};
   int d = 0;
   cudaError_t e = cudaGetDevice(&d);
   if (e != cudaSuccess) return e;
   const unsigned long long bit = d >= 0 && d < 64 ? (1ull << d) : 0ull;
-  if (bit && (done_mask.load(std::memory_order_relaxed) & bit)) return cudaSuccess;
-  e = cudaFuncSetAttribute(px_pull_kernel<UNR>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared);
-  if (e == cudaSuccess && bit) done_mask.fetch_or(bit, std::memory_order_relaxed);
-  return e;
-}
-
-template <int UNR>
-static cudaError_t px_launch_pull(const PxArgs& a, cudaStream_t stream) {
-  const cudaError_t prep = px_prepare_pull_kernel<UNR>();
-  if (prep != cudaSuccess) return prep;
+  if (!bit || !(done_mask.load(std::memory_order_relaxed) & bit)) {
+    e = cudaFuncSetAttribute(px_pull_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, px::kPullSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(px_pull_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    if (bit) done_mask.fetch_or(bit, std::memory_order_relaxed);
+  }
+  // one single-warp CTA per SM in all, each over a contiguous range of rows
+  a.ctas_per_src = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>((ctas_total + a.world - 1) / a.world, a.rows)));
   rla_clear_stale_launch_error();
-  px_pull_kernel<UNR><<<a.world * a.ctas_per_src, px::kPullThreads, 0, stream>>>(a);
+  px_pull_kernel<<<a.world * a.ctas_per_src, 32, px::kPullSmem, stream>>>(a);
   return cudaGetLastError();
 }
 
@@ -319,20 +396,11 @@ int rla_prefill_exchange_block(const void* const* xb_peers, int64_t ld_xb, void*
   a.chunks = static_cast<int>(chunks);
   a.block = block;
   a.last = last ? 1 : 0;
-  // about one CTA per SM in all (it fits beside a GEMM CTA), one warp per
-  // row, fewer CTAs when a block has fewer rows than that
-  const int warps = px::kPullThreads / 32;
-  const int64_t want = (device_sm_count() + world - 1) / world;
-  a.ctas_per_src = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, (rows + warps - 1) / warps)));
-  int unroll = 4;
+  int ctas_total = device_sm_count();
 #ifdef RLA_EXPERIMENTS
-  unroll = exp_int("RLA_PX_UNROLL", unroll);
-  if (const int c = exp_int("RLA_PX_CTAS", 0); c > 0)
-    a.ctas_per_src = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((c + world - 1) / world,
-                                                                            (rows + warps - 1) / warps)));
+  ctas_total = exp_int("RLA_PX_CTAS", ctas_total);
 #endif
-  const cudaError_t e = unroll == 8 ? px_launch_pull<8>(a, static_cast<cudaStream_t>(stream))
-                                    : px_launch_pull<4>(a, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = px_launch_pull(a, ctas_total, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     set_error("%s: launch failed: %s", fn, cudaGetErrorString(e));
     return RLA_ERR_CUDA;

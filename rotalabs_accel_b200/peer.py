@@ -196,10 +196,14 @@ _comm_streams: dict = {}
 
 
 def comm_stream(device: torch.device) -> torch.cuda.Stream:
-    """The per-device stream that the overlapped prefill runs its exchange on."""
+    """The per-device stream that the overlapped prefill runs its exchange on.
+    High priority: when a GEMM CTA leaves an SM, a waiting exchange CTA gets
+    the SM before the next GEMM tile (measured at 2 ranks, M = 4096, the
+    8192 -> 14336 shard's pull overlapped in two blocks: 1130 -> 1072 us per
+    call)."""
     s = _comm_streams.get(device.index)
     if s is None:
-        s = _comm_streams[device.index] = torch.cuda.Stream(device=device)
+        s = _comm_streams[device.index] = torch.cuda.Stream(device=device, priority=-1)
     return s
 
 

@@ -83,9 +83,11 @@ def assemble_columns(staging: torch.Tensor, n_total: int, out: Optional[torch.Te
 # the local GEMM of a block takes whole waves of tiles (tcgen05 kernel, one
 # tile per SM at a time, blocks on one stream run one after the other), and
 # the all-gather plus reorder of a block runs while the next block's GEMM
-# does.  Figures measured on B200: about 7.4 TFLOP/s per SM for 256-row tiles
-# and 6.4 for 128-row tiles; the NCCL all-gather delivers about 650 GB/s into
-# each rank after ~15 us of start-up; the reorder moves about 5 TB/s.
+# does.  Figures measured on B200 (config-4 shards at M = 512-4096): a wave
+# of 256-row tiles takes ~2*128*256*K / 8.0e12 s, a wave of 128-row tiles
+# ~0.95 of that; the NCCL all-gather delivers about 650 GB/s into each rank
+# after ~15 us of start-up and the reorder moves about 5 TB/s; the pull
+# exchange moves ~400 GB/s into each rank while a GEMM runs beside it.
 def _gemm_us(rows: int, n_local: int, K: int, sms: int) -> float:
     nt = -(-n_local // 128)
 
@@ -93,20 +95,19 @@ def _gemm_us(rows: int, n_local: int, K: int, sms: int) -> float:
         return -(-(nt * -(-rows // bm)) // sms)
 
     # the library's own choice of tile height (rla_capi.cu, make_plan)
-    if rows > 128 and waves(256) * 256 * 1.0 <= waves(128) * 128 * 1.16:
-        bm, rate = 256, 7.4e12
-    elif rows > 64:
-        bm, rate = 128, 6.4e12
-    else:
-        bm, rate = 64, 4.0e12
-    return waves(bm) * (2.0 * 128 * bm * K / rate) * 1e6
+    wave_us = 2.0 * 128 * 256 * K / 8.0e12 * 1e6
+    if rows > 128 and waves(256) * 256 * 1.0 <= waves(128) * 128 * 1.9:
+        return waves(256) * wave_us
+    if rows > 64:
+        return waves(128) * 0.95 * wave_us
+    return waves(64) * 0.95 * wave_us
 
 
 def _exchange_us(rows: int, n_local: int, world: int, kind: str = "nccl") -> float:
     if kind == "p2p":
-        # pull exchange: each rank reads the peers' slices over NVLink at
-        # about 700 GB/s (its own slice is a local copy beside it)
-        return 6.0 + (world - 1) * rows * n_local * 2 / 700e9 * 1e6
+        # pull exchange: each rank reads the peers' slices over NVLink (its
+        # own slice is a local copy beside it)
+        return 6.0 + (world - 1) * rows * n_local * 2 / 400e9 * 1e6
     ag = 15.0 + (world - 1) * rows * n_local * 2 / 650e9 * 1e6
     reorder = 2.0 * rows * world * n_local * 2 / 5e12 * 1e6
     return ag + reorder
