@@ -79,38 +79,78 @@ def assemble_columns(staging: torch.Tensor, n_total: int, out: Optional[torch.Te
     return out
 
 
-# Block sizes of the overlapped prefill, from a two-stream pipeline model:
-# the local GEMM of a block takes whole waves of tiles (tcgen05 kernel, one
-# tile per SM at a time, blocks on one stream run one after the other), and
-# the all-gather plus reorder of a block runs while the next block's GEMM
-# does.  Figures measured on B200 (config-4 shards at M = 512-4096): a wave
-# of 256-row tiles takes ~2*128*256*K / 8.0e12 s, a wave of 128-row tiles
-# ~0.95 of that; the NCCL all-gather delivers about 650 GB/s into each rank
-# after ~15 us of start-up and the reorder moves about 5 TB/s; the pull
-# exchange moves ~400 GB/s into each rank while a GEMM runs beside it.
+# Block sizes of the overlapped prefill, from a two-stream model fitted to
+# B200 measurements of the config-4 shards (M = 512-4096, 2 ranks):
+#  * the local GEMM of a block takes whole rounds of tiles (tcgen05 kernel,
+#    one tile per SM at a time; blocks on one stream run one after the
+#    other); a round of 256-row tiles takes ~7.8 us + K * 7.23 ns, a round of
+#    128-row tiles ~0.95 of that, a grid smaller than one round ~0.9 of it
+#    (fewer busy SMs under the power cap), plus ~8 us per launch;
+#  * the pull exchange moves ~600 GB/s into a rank alone and ~350 GB/s while
+#    a GEMM runs beside it, and slows that GEMM by a quarter of the overlap;
+#  * the NCCL path: ~15 us + ~650 GB/s of all-gather into each rank, then a
+#    reorder at ~5 TB/s.
 def _gemm_us(rows: int, n_local: int, K: int, sms: int) -> float:
     nt = -(-n_local // 128)
 
-    def waves(bm):
-        return -(-(nt * -(-rows // bm)) // sms)
+    def tiles(bm):
+        return nt * -(-rows // bm)
 
+    def rounds(bm):
+        return -(-tiles(bm) // sms)
+
+    round_us = 7.8 + K * 7.23e-3
     # the library's own choice of tile height (rla_capi.cu, make_plan)
-    wave_us = 2.0 * 128 * 256 * K / 8.0e12 * 1e6
-    if rows > 128 and waves(256) * 256 * 1.0 <= waves(128) * 128 * 1.9:
-        return waves(256) * wave_us
-    if rows > 64:
-        return waves(128) * 0.95 * wave_us
-    return waves(64) * 0.95 * wave_us
+    if rows > 128 and rounds(256) * 256 * 1.0 <= rounds(128) * 128 * 1.9:
+        bm, rel = 256, 1.0
+    elif rows > 64:
+        bm, rel = 128, 0.95
+    else:
+        bm, rel = 64, 0.95
+    if tiles(bm) < sms:
+        rel *= 0.9
+    return rounds(bm) * rel * round_us + 8.0
 
 
 def _exchange_us(rows: int, n_local: int, world: int, kind: str = "nccl") -> float:
+    """The exchange of one block alone (no GEMM beside it)."""
     if kind == "p2p":
-        # pull exchange: each rank reads the peers' slices over NVLink (its
-        # own slice is a local copy beside it)
-        return 6.0 + (world - 1) * rows * n_local * 2 / 400e9 * 1e6
+        return 6.0 + (world - 1) * rows * n_local * 2 / 600e9 * 1e6
     ag = 15.0 + (world - 1) * rows * n_local * 2 / 650e9 * 1e6
     reorder = 2.0 * rows * world * n_local * 2 / 5e12 * 1e6
     return ag + reorder
+
+
+def _pipeline_us(block_rows, n_local: int, K: int, world: int, sms: int, kind: str = "nccl") -> float:
+    """Modelled time of one call with these row blocks (see above)."""
+    if kind != "p2p":
+        t_gemm = t_done = 0.0
+        for r in block_rows:
+            t_gemm += _gemm_us(r, n_local, K, sms)
+            t_done = max(t_gemm, t_done) + _exchange_us(r, n_local, world, kind)
+        return t_done
+    r_alone, r_ovl, slow = 600e9, 350e9, 0.25
+    g_end, t = [], 0.0
+    for r in block_rows:
+        t += _gemm_us(r, n_local, K, sms)
+        g_end.append(t)
+    t_pull, extra = 0.0, 0.0
+    for i, r in enumerate(block_rows):
+        start = max(g_end[i] + extra, t_pull)
+        nbytes = (world - 1) * r * n_local * 2
+        if i + 1 < len(block_rows):
+            window = max(0.0, g_end[i + 1] + extra - start)
+            d_ovl = nbytes / r_ovl * 1e6
+            if d_ovl <= window:
+                dur = d_ovl
+                extra += slow * dur
+            else:
+                dur = window + (nbytes - window * 1e-6 * r_ovl) / r_alone * 1e6
+                extra += slow * window
+        else:
+            dur = nbytes / r_alone * 1e6
+        t_pull = start + dur + 6.0
+    return max(t_pull, g_end[-1] + extra)
 
 
 def _compositions(units: int, parts: int):
@@ -126,17 +166,15 @@ def _compositions(units: int, parts: int):
 def prefill_row_blocks(M: int, n_local: int, K: int = 8192, world: int = 2, sms: int = 148, exchange: str = "nccl"):
     """``[(row0, rows), ...]`` covering ``[0, M)`` in order: 1 to 4 blocks of
     rows, each a multiple of 128 rows but the last (which takes the ragged
-    tail, so no block is shorter than 128 rows unless M is), with the least
-    modelled time.  Blocks need not be equal: a GEMM whose tiles end in a partial wave
-    is cut where the waves are full (e.g. 13 + 3 row tiles of 256 rows for a
-    4096 x 14336 shard on 148 SMs), so the blocks cost no more GEMM waves than
-    the whole, and the short last block leaves little exchange exposed.  One
-    block is the serial GEMM -> all-gather -> reorder; more blocks are taken
-    only for a clear gain (3 %).  ``exchange``: "nccl" (all-gather, then
-    reorder) or "p2p" (``PrefillExchange``'s pull over NVLink)."""
+    tail), at least 512 rows each when there are several, with the least
+    modelled time (``_pipeline_us``).  Blocks need not be equal: a block
+    split that adds a partly empty round of tiles costs GEMM time (4096 x
+    14336 on 148 SMs is 12.1 rounds; halves are 6.05 each, but 3328 + 768 rows
+    are 10 + 3), and a short last block leaves little exchange exposed.  One
+    block is the serial GEMM -> exchange; more blocks are taken only for a
+    clear gain (3 %).  ``exchange``: "nccl" (all-gather, then reorder) or
+    "p2p" (``PrefillExchange``'s pull over NVLink)."""
     units = max(1, M // 128)     # a ragged tail of rows joins the last block
-    gemm = {}
-    comm = {}
 
     def rows_of(u0, u):
         return M - u0 * 128 if u0 + u == units else u * 128
@@ -145,19 +183,16 @@ def prefill_row_blocks(M: int, n_local: int, K: int = 8192, world: int = 2, sms:
     for c in range(1, min(4, units) + 1):
         c_best, c_t = None, None
         for comp in _compositions(units, c):
-            t_gemm = t_done = 0.0
-            u0 = 0
+            if c > 1 and min(comp) < 4:      # blocks of 512 rows or more (the model is fitted there)
+                continue
+            rows, u0 = [], 0
             for u in comp:
-                r = rows_of(u0, u)
-                if r not in gemm:
-                    gemm[r] = _gemm_us(r, n_local, K, sms)
-                    comm[r] = _exchange_us(r, n_local, world, exchange)
-                t_gemm += gemm[r]
-                t_done = max(t_gemm, t_done) + comm[r]
+                rows.append(rows_of(u0, u))
                 u0 += u
-            if c_t is None or t_done < c_t:
-                c_best, c_t = comp, t_done
-        if best_t is None or c_t < best_t * 0.97:
+            t = _pipeline_us(rows, n_local, K, world, sms, exchange)
+            if c_t is None or t < c_t:
+                c_best, c_t = comp, t
+        if c_t is not None and (best_t is None or c_t < best_t * 0.97):
             best, best_t = c_best, c_t
     blocks, u0 = [], 0
     for u in best:
