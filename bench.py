@@ -418,6 +418,17 @@ def measure_sharded(ra, _capi, dist, dev, world, rank, capture, timed, peaks, ar
             entry = {"us": round(ms_gemm * 1e3, 2), "steps": steps,
                      "parity": {"max_abs_err": round(abs_err, 6), "max_err_over_max1_ref": round(rel_err, 6),
                                 "rows_checked": rows_checked, "ok": ok}}
+            if world > 1:
+                # this rank's shard GEMM alone (no exchange), same weights and
+                # steps: the exchange's cost is us - local_gemm_us
+                def fn_local():
+                    for (q, sc) in use:
+                        _capi.w8a16_gemm(x, q, sc, None, out=y_local)
+
+                gph = capture(fn_local)
+                ms_l, _ = timed(gph, steps, args.warmup)
+                del gph
+                entry["local_gemm_us"] = round(ms_l / len(use) * 1e3, 2)
             if prefill:
                 tf = 2.0 * M * N * K / (ms_gemm * 1e-3) / 1e12
                 entry.update({"value": round(tf, 1), "unit": "TFLOP/s",

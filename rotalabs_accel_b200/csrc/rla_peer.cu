@@ -162,6 +162,11 @@ int rla_w8a16_gemm_allgather(const void* x, int64_t ldx, const int8_t* w, int64_
     return RLA_ERR_UNSUPPORTED;
   }
   const int64_t slot_words = ((M + 1) / 2) * n_local;
+  if ((int64_t)world * slot_words >= (int64_t(1) << 32)) {
+    set_error("rla_w8a16_gemm_allgather: %d ranks x %lld flagged words per slice exceed 2^32",
+              world, (long long)slot_words);
+    return RLA_ERR_UNSUPPORTED;
+  }
   const int64_t half_words = static_cast<int64_t>(recv_bytes / 16);
   if ((int64_t)world * slot_words > half_words) {
     set_error("rla_w8a16_gemm_allgather: receive buffers of %zu bytes hold less than 2 x %d x %lld flagged words",

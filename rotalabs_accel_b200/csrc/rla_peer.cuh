@@ -113,13 +113,24 @@ RLA_DEVFN bool peer_wait_word(const PeerOut& po, const uint2* w, unsigned int s,
 }
 
 // One received flagged word (pair p, column n of source rank src; pc = p *
-// n_local + n) into y.
-RLA_DEVFN void peer_unpack_word(uint2 v, __half* y, int64_t ldy, int M, int n_local, int src, int64_t pc) {
-  const int p = static_cast<int>(pc / n_local);
-  const int n = static_cast<int>(pc - (int64_t)p * n_local);
+// n_local + n < 2^31) into y.
+RLA_DEVFN void peer_unpack_word(uint2 v, __half* y, int64_t ldy, int M, int n_local, int src, uint32_t pc) {
+  const uint32_t p = pc / static_cast<uint32_t>(n_local);
+  const uint32_t n = pc - p * static_cast<uint32_t>(n_local);
   const int64_t col = (int64_t)src * n_local + n;
   y[(int64_t)(2 * p) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x & 0xffffu));
-  if (2 * p + 1 < M) y[(int64_t)(2 * p + 1) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x >> 16));
+  if (2 * (int)p + 1 < M) y[(int64_t)(2 * p + 1) * ldy + col] = __ushort_as_half(static_cast<unsigned short>(v.x >> 16));
+}
+// Two received words of consecutive columns n, n + 1 (n even, same pair p)
+// into y as two 4-byte stores (y's rows and columns are 4-byte aligned:
+// ldy and the column are even).
+RLA_DEVFN void peer_unpack_word2(uint2 a, uint2 b, __half* y, int64_t ldy, int M, int n_local, int src, uint32_t pc) {
+  const uint32_t p = pc / static_cast<uint32_t>(n_local);
+  const uint32_t n = pc - p * static_cast<uint32_t>(n_local);
+  const int64_t col = (int64_t)src * n_local + n;
+  *reinterpret_cast<uint32_t*>(y + (int64_t)(2 * p) * ldy + col) = (a.x & 0xffffu) | (b.x << 16);
+  if (2 * (int)p + 1 < M)
+    *reinterpret_cast<uint32_t*>(y + (int64_t)(2 * p + 1) * ldy + col) = (a.x >> 16) | (b.x & 0xffff0000u);
 }
 
 // Phase 2.  Called by the `nthreads` threads of a CTA that take part in named
@@ -170,23 +181,31 @@ RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t
   // loads before it looks at any flag; a word whose flag is not yet s is then
   // waited for on its own.
   const int wpu = (po.half_words % 2 == 0 && per_src % 2 == 0) ? 2 : 1;
-  const int64_t units = total / wpu;
-  const int64_t stride = (int64_t)R * nthreads;
+  // Two words of one unit are columns n, n + 1 of one pair when n_local is
+  // even (per_src even and every unit starts on an even word); they then go
+  // to y as 4-byte stores when y's rows keep 4-byte alignment.
+  const bool store2 = wpu == 2 && n_local % 2 == 0 && ldy % 2 == 0 && (reinterpret_cast<uintptr_t>(y) & 3u) == 0;
+  // Index arithmetic in 32 bits: the host limits M to 32 and n_local to
+  // 2^31, and total = pairs * n_local * (world - 1) < 2^32 for every
+  // decode shard (16 * 28672 * 7 words at most in the 70B layers).
+  const uint32_t units = static_cast<uint32_t>(total / wpu);
+  const uint32_t per_src32 = static_cast<uint32_t>(per_src);
+  const uint32_t stride = R * static_cast<uint32_t>(nthreads);
   constexpr int kBatch = 4;
   bool live = !poisoned;
-  for (int64_t base = (int64_t)u * nthreads + tid; live && base < units; base += kBatch * stride) {
+  for (uint32_t base = static_cast<uint32_t>(u) * nthreads + tid; live && base < units; base += kBatch * stride) {
     uint2 v[kBatch][2];
     int src[kBatch];
-    int64_t pc[kBatch];
+    uint32_t pc[kBatch];
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
-      const int64_t unit = base + b * stride;
+      const uint32_t unit = base + b * stride;
       src[b] = -1;
       if (unit < units) {
-        const int64_t w = unit * wpu;
-        const int si = static_cast<int>(w / per_src);
+        const uint32_t w = unit * wpu;
+        const int si = static_cast<int>(w / per_src32);
         src[b] = si < po.rank ? si : si + 1;
-        pc[b] = w - (int64_t)si * per_src;
+        pc[b] = w - static_cast<uint32_t>(si) * per_src32;
         const uint2* a = peer_word(po, po.rank, s, src[b], pc[b]);
         if (wpu == 2) rla_ld_flagged2(a, v[b][0], v[b][1]);
         else v[b][0] = rla_ld_flagged(a);
@@ -196,12 +215,16 @@ RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t
     for (int b = 0; b < kBatch; ++b) {
       if (src[b] < 0 || !live) continue;
       for (int j = 0; j < wpu; ++j) {
-        uint2 word = v[b][j];
-        if (word.y != s && !peer_wait_word(po, peer_word(po, po.rank, s, src[b], pc[b] + j), s, word, t0)) {
+        if (v[b][j].y != s && !peer_wait_word(po, peer_word(po, po.rank, s, src[b], pc[b] + j), s, v[b][j], t0)) {
           live = false;
           break;
         }
-        peer_unpack_word(word, y, ldy, M, n_local, src[b], pc[b] + j);
+      }
+      if (!live) break;
+      if (store2) {
+        peer_unpack_word2(v[b][0], v[b][1], y, ldy, M, n_local, src[b], pc[b]);
+      } else {
+        for (int j = 0; j < wpu; ++j) peer_unpack_word(v[b][j], y, ldy, M, n_local, src[b], pc[b] + j);
       }
     }
   }
