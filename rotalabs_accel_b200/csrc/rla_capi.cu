@@ -244,8 +244,12 @@ static Plan make_plan_uncached(int64_t M, int64_t N, int64_t K, bool aligned, bo
     // For M <= 8 the skinny kernel now wins on large layers too (M = 1:
     // 8192 -> 28672 skinny 40.9 us vs stream 45.2; 28672 -> 8192 39.0 vs
     // 45.3); at M = 16 the stream kernel keeps them (55.9 vs 64.9 us).
+    // Its exchange form (56-64 registers at M <= 8 since the unpacking uses
+    // 32-bit index arithmetic) also wins there: two ranks, the config-4
+    // shards of 117 MB, M = 1: 30.2 vs 31.5 us (8192 -> 14336) and 31.2 vs
+    // 33.0 us (28672 -> 4096); M = 8: 31.3 vs 32.4 and 31.8 vs 33.5 us.
     const bool stream_wins =
-        M <= 16 && (peer ? ((M > 8 && wbytes >= 25e6) || wbytes >= 100e6)
+        M <= 16 && (peer ? (M > 8 && wbytes >= 25e6)
                          : (M > 8 && ((wbytes >= 40e6 && multi_wave) || wbytes >= 120e6)));
     const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
     // The stream kernel keeps one arrival counter per CTA in the counter region.
