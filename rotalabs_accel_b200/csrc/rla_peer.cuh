@@ -10,10 +10,12 @@
 //    d's receive buffer.  An aligned 8-byte store is seen whole or not at
 //    all, so a reader that finds the flag s in a word has its data: no fence,
 //    no separate completion flag (the low-latency protocol NCCL calls LL).
-//  * Phase 2 (unpacking).  Every CTA takes a ticket when its phase 1 is done.
-//    The last R CTAs to finish wait until all CTAs of the launch have taken
-//    one, then poll the receive buffer for every peer's words of call s and
-//    write them into y.  When the kernel completes, y holds all slices.
+//  * Phase 2 (unpacking).  When the whole grid is resident at once, every
+//    CTA unpacks its share right after its own phase 1.  Otherwise every CTA
+//    takes a ticket when its phase 1 is done, and the last R CTAs to finish
+//    wait until all CTAs of the launch have taken one.  Unpacking CTAs poll
+//    the receive buffer for every peer's words of call s and write them into
+//    y.  When the kernel completes, y holds all slices.
 //
 // Reuse without a handshake: receive buffers are double-buffered by the
 // parity of s.  A rank writes a peer's parity-p half in call s only after its
@@ -23,10 +25,13 @@
 // comes after the kernel's dependency wait, so this holds with programmatic
 // dependent launch too.)
 //
-// No cross-GPU deadlock: a CTA waits on peers only after every CTA of its own
-// launch has finished phase 1, and phase 1 waits on nothing outside the GPU.
-// Inside the GPU, R <= (resident CTAs + 1) / 2 (or the whole grid when it is
-// resident at once) leaves room for every CTA that has not yet run.
+// No cross-GPU deadlock: phase 1 waits on nothing outside the GPU.  With the
+// whole grid resident, every CTA of a launch runs its phase 1 whatever the
+// others wait for.  Otherwise a CTA waits on peers only after every CTA of
+// its own launch has finished phase 1, and R <= (resident CTAs + 1) / 2
+// leaves room for every CTA that has not yet run.  (Programmatic dependent
+// launch does not change this: a dependent grid starts only after every CTA
+// of this grid has started.)
 //
 // The call number s is one more than the calls this rank has completed (a
 // counter in its sync area, advanced by the last unpacking CTA).  Every wait is
@@ -147,9 +152,19 @@ RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
   const unsigned int ctas = gridDim.x * gridDim.y;
   const unsigned int R = po.unpackers;
+  // When the whole grid is resident at once (R == ctas) every CTA unpacks as
+  // soon as its own phase 1 is done: no CTA of this launch can be kept from
+  // running by the waiting ones, so the grid-wide arrival wait (and the
+  // polling of one counter by every CTA, which slows the arrivals themselves)
+  // is not needed; a CTA's share follows from its index.
+  const bool resident_grid = R == ctas;
   if (tid == 0) {
-    const unsigned int ticket = atomicAdd(po.sync + kSyncArrive, 1u);
-    *slot = ticket >= ctas - R ? static_cast<int>(ticket - (ctas - R)) : -1;
+    if (resident_grid) {
+      *slot = static_cast<int>(blockIdx.y * gridDim.x + blockIdx.x);
+    } else {
+      const unsigned int ticket = atomicAdd(po.sync + kSyncArrive, 1u);
+      *slot = ticket >= ctas - R ? static_cast<int>(ticket - (ctas - R)) : -1;
+    }
   }
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
   const int u = *slot;
@@ -159,7 +174,7 @@ RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t
   if (tid == 0) {
     if (poisoned) {
       rla_record_error(RLA_DEVERR_PEER_POISONED);
-    } else {
+    } else if (!resident_grid) {
       // Wait until every CTA of the launch has finished phase 1.
       while (rla_ld_relaxed_gpu_u32(po.sync + kSyncArrive) < ctas) {
         if (rla_ld_relaxed_gpu_u32(po.sync + kSyncAbort) != 0u) break;
