@@ -248,9 +248,15 @@ static Plan make_plan_uncached(int64_t M, int64_t N, int64_t K, bool aligned, bo
     // 32-bit index arithmetic) also wins there: two ranks, the config-4
     // shards of 117 MB, M = 1: 30.2 vs 31.5 us (8192 -> 14336) and 31.2 vs
     // 33.0 us (28672 -> 4096); M = 8: 31.3 vs 32.4 and 31.8 vs 33.5 us.
+    // At M = 9..16 the skinny exchange form (no grid-wide wait when its grid
+    // is resident) wins on shards that fit one wave up to ~100 MB (one GPU,
+    // world-1 exchange, M = 16: 8192 -> 3584 skinny 15.6 us vs stream 18.5;
+    // 28672 -> 1024 16.1 vs 25.6), the stream form from 100 MB (two ranks,
+    // M = 16: 28672 -> 4096 50.4 vs 39.6 us; 8192 -> 14336 68.2 vs 39.1).
     const bool stream_wins =
-        M <= 16 && (peer ? (M > 8 && wbytes >= 25e6)
-                         : (M > 8 && ((wbytes >= 40e6 && multi_wave) || wbytes >= 120e6)));
+        M <= 16 && M > 8 &&
+        (peer ? (wbytes >= 100e6 || (wbytes >= 40e6 && multi_wave))
+              : ((wbytes >= 40e6 && multi_wave) || wbytes >= 120e6));
     const bool want_stream = choice == RLA_KERNEL_STREAM || (choice == RLA_KERNEL_NONE && stream_wins);
     // The stream kernel keeps one arrival counter per CTA in the counter region.
     if (have_workspace && want_stream && sms <= kMaxSplitRowBlocks) {
