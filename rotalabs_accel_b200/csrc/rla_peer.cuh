@@ -257,4 +257,16 @@ RLA_DEVFN void peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t
   }
 }
 
+// The same phase as an out-of-line call.  The decode kernel's forms with two
+// or more token tiles use it: with the unpacking code kept out of the
+// kernel body, the compiler's register choice for the GEMM part runs them
+// faster (one GPU, world-1 exchange, M = 16: 8192 -> 14336 65-73 -> 46 us,
+// 28672 -> 4096 48-51 -> 40 us, 8192 -> 3584 15.6-17.3 -> 14.0 us,
+// 28672 -> 1024 16.0-16.5 -> 15.1 us), while the one-tile forms run slower
+// that way (M = 1: 28.8 -> 41.9 us on 8192 -> 14336) and keep it inline.
+__device__ __noinline__ void peer_finish_call(const PeerOut& po, unsigned int s, __half* y, int64_t ldy, int M,
+                                              int n_local, int tid, int nthreads, int bar_id, int* slot) {
+  peer_finish(po, s, y, ldy, M, n_local, tid, nthreads, bar_id, slot);
+}
+
 }  // namespace rla

@@ -66,6 +66,16 @@ RLA_DEVFN void skinny_chunk_mma(float (&acc)[NT][4], const uint4 (&wa)[2], const
   }
 }
 
+// The unpacking phase of the exchange form: out of line for two or more
+// token tiles (see peer_finish_call).
+template <int NT>
+RLA_DEVFN void skinny_peer_finish(const PeerOut& po, unsigned int s, __half* y, int64_t ldy, int M, int N, int* slot) {
+  if constexpr (NT >= 2)
+    peer_finish_call(po, s, y, ldy, M, N, threadIdx.x, blockDim.x, 0, slot);
+  else
+    peer_finish(po, s, y, ldy, M, N, threadIdx.x, blockDim.x, 0, slot);
+}
+
 template <int NT, int WN, int WK, int U, bool PEER, bool GLU, bool XJ>
 RLA_DEVFN void skinny_body(const __half* __restrict__ x, int64_t ldx, const int8_t* __restrict__ w, int64_t ldw,
                            const void* __restrict__ scale, int scale_f32, const void* __restrict__ bias,
@@ -244,7 +254,7 @@ RLA_DEVFN void skinny_body(const __half* __restrict__ x, int64_t ldx, const int8
     }
     rla_cluster_sync();  // no CTA exits while rank 0 may still read its shared memory
     if (rank != 0) {
-      if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
+      if constexpr (PEER) skinny_peer_finish<NT>(po, call, y, ldy, M, N, &peer_slot);
       return;
     }
   }
@@ -302,7 +312,7 @@ RLA_DEVFN void skinny_body(const __half* __restrict__ x, int64_t ldx, const int8
         }
       }
     }
-    if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
+    if constexpr (PEER) skinny_peer_finish<NT>(po, call, y, ldy, M, N, &peer_slot);
     return;
   }
 
@@ -334,7 +344,7 @@ RLA_DEVFN void skinny_body(const __half* __restrict__ x, int64_t ldx, const int8
   }
   __syncthreads();
   if (!is_last) {
-    if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
+    if constexpr (PEER) skinny_peer_finish<NT>(po, call, y, ldy, M, N, &peer_slot);
     return;
   }
 
@@ -388,7 +398,7 @@ RLA_DEVFN void skinny_body(const __half* __restrict__ x, int64_t ldx, const int8
     }
   }
   if (threadIdx.x == 0) counters[blockIdx.x] = 0u;  // leave the workspace re-usable
-  if constexpr (PEER) peer_finish(po, call, y, ldy, M, N, threadIdx.x, blockDim.x, 0, &peer_slot);
+  if constexpr (PEER) skinny_peer_finish<NT>(po, call, y, ldy, M, N, &peer_slot);
 }
 
 #define RLA_SKINNY_PARAMS                                                                                     \
