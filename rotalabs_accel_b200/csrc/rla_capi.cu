@@ -82,8 +82,11 @@ static void skinny_shape(Plan& p, int64_t M, int64_t N, int64_t K, bool have_ws,
     p.wk = 4;
   // Long K at M <= 8: 128-thread CTAs with twice the K slices.  Measured on
   // B200 at M = 1: 28672 -> 8192 49.8 -> 39.0 us, 28672 -> 1024 9.8 -> 8.5 us,
-  // 8192 -> 3584 9.1 -> 8.2 us; not at 11008 -> 4096 (12.0 -> 12.6 us).
-  if (!gated && !peer && p.nt == 1 && p.wn == 1 && p.wk == 8 && (K >= 16384 || (K >= 8192 && N < 4096)))
+  // 8192 -> 3584 9.1 -> 8.2 us; not at 11008 -> 4096 (12.0 -> 12.6 us).  The
+  // exchange form takes it for narrow shards only (one GPU, world-1
+  // exchange, M = 1: 28672 -> 1024 11.5 -> 10.6 us, 8192 -> 3584 10.8 ->
+  // 10.5 us; 28672 -> 4096 28.6 -> 29.6 us, so not there).
+  if (!gated && p.nt == 1 && p.wn == 1 && p.wk == 8 && ((K >= 16384 && !peer) || (K >= 8192 && N < 4096)))
     p.wk = 4;
   // M <= 8 on layers of at most two row blocks per SM (but more than one):
   // one 512-thread CTA of 16 k-warps per row block (two resident per SM),

@@ -416,6 +416,16 @@ __global__ void __launch_bounds__(32 * WN * WK) w8a16_skinny_kernel(RLA_SKINNY_P
   skinny_body<NT, WN, WK, U, PEER, GLU, XJ>(RLA_SKINNY_ARGS);
 }
 
+// The one-tile exchange form of the 128-thread CTA with the register budget
+// of seven resident CTAs per SM: left to itself the compiler gives that form
+// 56 registers, too few to keep a whole batch of loads in flight (the plain
+// form gets 72); with this bound it gets 72.  One GPU, world-1 exchange,
+// 8192 -> 14336 at M = 1: 28.7 -> 24.6 us.
+template <int NT, int WN, int WK, int U, bool PEER, bool GLU, bool XJ>
+__global__ void __launch_bounds__(32 * WN * WK, 7) w8a16_skinny_kernel_b7(RLA_SKINNY_PARAMS) {
+  skinny_body<NT, WN, WK, U, PEER, GLU, XJ>(RLA_SKINNY_ARGS);
+}
+
 // One row group of 16 k-warps (512 threads) with the register budget of two
 // resident CTAs per SM (64 registers): for M <= 8 on layers of at most two
 // row blocks per SM, every warp's K share is in flight in one batch of loads
@@ -453,9 +463,12 @@ struct SkinnyInst {
       (void)form;  // plain form only (the plan never asks for the others)
       return w8a16_skinny16_kernel<NT, U, XJ>;
     } else {
-      return form == 1   ? w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>
-             : form == 2 ? w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>
-                         : w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>;
+      if (form == 2) {
+        if constexpr (NT == 1 && WN * WK == 4) return w8a16_skinny_kernel_b7<NT, WN, WK, U, true, false, XJ>;
+        return w8a16_skinny_kernel<NT, WN, WK, U, true, false, XJ>;
+      }
+      return form == 1 ? w8a16_skinny_kernel<NT, WN, WK, U, false, true, XJ>
+                       : w8a16_skinny_kernel<NT, WN, WK, U, false, false, XJ>;
     }
   }
   // CTAs that can be resident on the whole device at once when the K slices
