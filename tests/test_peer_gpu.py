@@ -35,6 +35,11 @@ pytestmark = pytest.mark.gpu
 
 SHAPES = [(1, 4096, 4096), (4, 1376, 4096), (8, 2048, 11008), (16, 7168, 4096), (3, 100, 96), (32, 512, 256),
           (5, 7168, 4096)]
+# The 70B MLP shards at 2 and 8 ranks (their exchange plans: the one-tile
+# 128-thread form with its own register budget, the long-K plan of narrow
+# shards, the two-tile form with out-of-line unpacking).
+SHARD_SHAPES = [(1, 14336, 8192), (8, 4096, 28672), (1, 3584, 8192), (8, 1024, 28672), (16, 3584, 8192),
+                (16, 1024, 28672)]
 
 
 def _free_port():
@@ -73,16 +78,16 @@ def _close(a, b):
     return float((a - b).abs().max()) <= 1e-2 * max(1.0, float(b.abs().max()))
 
 
-@pytest.mark.parametrize("kernel", ["skinny", "stream"])
+@pytest.mark.parametrize("kernel", ["skinny", "stream", "auto"])
 def test_world1_fused_equals_plain(single_rank_group, kernel):
     from rotalabs_accel_b200 import _capi
     from rotalabs_accel_b200.peer import PeerExchange
     _capi.set_decode_kernel(kernel)
-    ex = PeerExchange(max_rows=32, max_n_local=8192)
+    ex = PeerExchange(max_rows=32, max_n_local=14336)
     try:
         calls0 = ex.calls_completed()
         n_calls = 0
-        for i, (M, N, K) in enumerate(SHAPES):
+        for i, (M, N, K) in enumerate(SHAPES + (SHARD_SHAPES if kernel == "auto" else [])):
             x, q, s, b = _problem(M, N, K, 100 + i, bias=(i % 2 == 1))
             ref = _capi.w8a16_gemm(x, q, s, b)
             out = torch.full((M, N + 8), float("nan"), dtype=torch.float16, device="cuda")   # ldy > N
