@@ -482,7 +482,8 @@ def run_case(case: str) -> int:
     N=28672; ``decode-large16`` 2 of M=16 on that shape; ``skinny16`` 3
     launches of the skinny kernel at M=16, K=4096, N=14336; ``prefill`` 2
     launches of M=2048, K=4096, N=11008; ``mlp8`` / ``mlp2048`` 2 gated
-    gate/up GEMMs of config 3."""
+    gate/up GEMMs of config 3; ``exchange1`` the 8192 -> 14336 shard at M=1,
+    2 plain launches then 2 world-1 fused-exchange launches."""
     import torch
     import rotalabs_accel_b200 as ra
     from rotalabs_accel_b200 import _capi
@@ -527,12 +528,129 @@ def run_case(case: str) -> int:
         _, qu, su = prob(1, 11008, 4096, 1)
         for _ in range(2):
             _capi.w8a16_gemm_swiglu(x, qg, sg, qu, su)
+    elif case == "exchange1":
+        # the same shard through the plain decode GEMM (2 launches) and the
+        # world-1 fused exchange form (2 launches), for a side-by-side capture
+        import datetime
+        import torch.distributed as dist
+        from rotalabs_accel_b200.peer import PeerExchange
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29561")
+        dist.init_process_group("gloo", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
+        ex = PeerExchange(max_rows=16, max_n_local=14336)
+        x, q, s = prob(1, 14336, 8192, 0)
+        y = torch.empty(1, 14336, device=dev, dtype=torch.float16)
+        for _ in range(2):
+            _capi.w8a16_gemm(x, q, s, None, out=y)
+        torch.cuda.synchronize()
+        for _ in range(2):
+            ex.gemm(x, q, s, None, out=y)
+        torch.cuda.synchronize()
+        ex.close()
+        dist.destroy_process_group()
     else:
         raise SystemExit(f"unknown case {case}")
     torch.cuda.synchronize()
     err = _capi.device_error()
     print("case", case, "device_error", err)
     return 0 if err == 0 else 1
+
+
+def run_prefill_timeline() -> int:
+    """``--case prefill-timeline`` (under torchrun, one rank per GPU): the
+    column-parallel prefill of config 4 (M = 4096, both 70B MLP shapes) with
+    the pull exchange, per candidate split of the rows into blocks (the
+    block model's pick and fixed ones), eager calls with CUDA events around
+    every GEMM block (compute stream) and every pull (communication stream);
+    medians of 8 calls, the call total as max over ranks.  Rank 0 prints one
+    JSON object."""
+    import datetime
+    import statistics
+    import torch
+    import torch.distributed as dist
+    import rotalabs_accel_b200 as ra
+    from rotalabs_accel_b200 import _capi
+    from rotalabs_accel_b200.peer import PrefillExchange, comm_stream
+    from rotalabs_accel_b200.sharded import prefill_row_blocks
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    else:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29563")
+        dist.init_process_group("gloo", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
+    M = SHARDED_PREFILL_M
+    pex = PrefillExchange(max_rows=M, max_n_local=max(N for (_, N) in SHARDED_KN) // world)
+    out = {"world": world, "M": M}
+
+    def mk(sizes):
+        blocks, r = [], 0
+        for z in sizes:
+            blocks.append((r, z))
+            r += z
+        return blocks
+
+    for (K, N) in SHARDED_KN:
+        nl = N // world
+        g = torch.Generator(device=dev).manual_seed(1 + rank)
+        q, sc = ra.quantize_weight_per_channel(torch.randn(nl, K, generator=g, device=dev) * 0.02)
+        sc = sc.half()
+        x = torch.randn(M, K, generator=g, device=dev).half()
+        y = torch.empty(M, N, device=dev, dtype=torch.float16)
+        xb = pex._xb_flat[:M * nl].view(M, nl)
+        cur, comm = torch.cuda.current_stream(dev), comm_stream(dev)
+        model = prefill_row_blocks(M, nl, K, world, _capi.device_sm_count(dev.index), "p2p")
+        cands = [model, mk([M]), mk([2048, 2048]), mk([3328, 768]), mk([2304, 1280, 512]), mk([1024] * 4),
+                 mk([2560, 1536])]
+        seen = set()
+        for blocks in cands:
+            key = tuple(r for _, r in blocks)
+            if key in seen:
+                continue
+            seen.add(key)
+            rec = {"total": [], "gemm": [[] for _ in blocks], "pull": [[] for _ in blocks]}
+            for it in range(10):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 + 3 * len(blocks))]
+                dist.barrier()
+                torch.cuda.synchronize()
+                ev[0].record(cur)
+                _capi.prefill_exchange_begin(pex._sync.ptrs, rank, cur.cuda_stream)
+                for b, (r0, rows) in enumerate(blocks):
+                    _capi.w8a16_gemm(x[r0:r0 + rows], q, sc, None, out=xb[r0:r0 + rows])
+                    ev[2 + 3 * b].record(cur)
+                    comm.wait_event(ev[2 + 3 * b])
+                    ev[3 + 3 * b].record(comm)
+                    _capi.prefill_exchange_block(pex._xb.ptrs, nl, pex._sync.ptrs, rank, b, b == len(blocks) - 1,
+                                                 r0, rows, nl, y, comm.cuda_stream)
+                    ev[4 + 3 * b].record(comm)
+                cur.wait_stream(comm)
+                ev[1].record(cur)
+                torch.cuda.synchronize()
+                if it < 2:
+                    continue
+                rec["total"].append(ev[0].elapsed_time(ev[1]) * 1e3)
+                prev = ev[0]
+                for b in range(len(blocks)):
+                    rec["gemm"][b].append(prev.elapsed_time(ev[2 + 3 * b]) * 1e3)
+                    prev = ev[2 + 3 * b]
+                    rec["pull"][b].append(ev[3 + 3 * b].elapsed_time(ev[4 + 3 * b]) * 1e3)
+            t = torch.tensor([statistics.median(rec["total"])], device=dev, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            out[f"{K}->{N} {list(key)}{' (model)' if blocks == model else ''}"] = {
+                "total_us": round(t.item(), 1),
+                "gemm_us": [round(statistics.median(v), 1) for v in rec["gemm"]],
+                "pull_us": [round(statistics.median(v), 1) for v in rec["pull"]]}
+        del q, sc, x, y
+        torch.cuda.empty_cache()
+    pex.check()
+    pex.close()
+    if rank == 0:
+        print(json.dumps(out))
+    dist.destroy_process_group()
+    return 0
 
 
 def main():
@@ -549,9 +667,12 @@ def main():
     ap.add_argument("--no-sharded", action="store_true", help="skip the config 4 column-parallel measurement")
     ap.add_argument("--no-mlp", action="store_true", help="skip the config 3 MLP block measurement")
     ap.add_argument("--case", choices=("sweep", "decode", "decode-large", "decode-large16", "skinny16", "prefill",
-                                       "mlp8", "mlp2048"),
-                    help="run one small fixed workload for a profiler capture and exit")
+                                       "mlp8", "mlp2048", "exchange1", "prefill-timeline"),
+                    help="run one small fixed workload for a profiler capture and exit (prefill-timeline: the "
+                         "per-block event timeline of the column-parallel prefill, under torchrun)")
     args = ap.parse_args()
+    if args.case == "prefill-timeline":
+        return run_prefill_timeline()
     if args.case:
         return run_case(args.case)
     if args.warmup < 3:
