@@ -57,6 +57,35 @@ def receive_bytes(world: int, max_rows: int, max_n_local: int) -> int:
     return 16 * world * ((max_rows + 1) // 2) * max_n_local
 
 
+def check_exchange_operands(x2d: torch.Tensor, weight_int8: torch.Tensor, scale: torch.Tensor,
+                            bias: Optional[torch.Tensor], out: Optional[torch.Tensor], world: int) -> None:
+    """The exchanges hand raw pointers to the library: refuse operands the
+    kernels would misread (``x2d`` fp16 ``[M, K]`` with unit inner stride,
+    ``weight_int8`` int8 ``[n_local, K]`` with unit inner stride, ``scale``
+    and ``bias`` contiguous ``[n_local]`` fp32/fp16, ``out`` fp16
+    ``[M, >= world * n_local]`` with unit inner stride, all on one CUDA
+    device)."""
+    if x2d.dim() != 2 or x2d.dtype != torch.float16 or not x2d.is_cuda or (x2d.numel() and x2d.stride(1) != 1):
+        raise TypeError("exchange: x must be a 2-D float16 CUDA tensor with unit inner stride")
+    dev = x2d.device
+    if (weight_int8.dim() != 2 or weight_int8.dtype != torch.int8 or weight_int8.device != dev
+            or weight_int8.shape[1] != x2d.shape[1] or (weight_int8.numel() and weight_int8.stride(1) != 1)):
+        raise TypeError(f"exchange: weight_int8 must be int8 [n_local, {x2d.shape[1]}] with unit inner stride on "
+                        f"{dev}")
+    n_local = weight_int8.shape[0]
+    for name, t in (("scale", scale), ("bias", bias)):
+        if t is None:
+            continue
+        if (t.shape != (n_local,) or t.dtype not in (torch.float16, torch.float32) or t.device != dev
+                or not t.is_contiguous()):
+            raise TypeError(f"exchange: {name} must be a contiguous float16/float32 [{n_local}] tensor on {dev}")
+    if out is not None and (out.dtype != torch.float16 or out.device != dev or out.dim() != 2
+                            or out.shape[0] != x2d.shape[0] or out.shape[1] < world * n_local
+                            or (out.numel() and out.stride(1) != 1)):
+        raise TypeError(f"exchange: out must be float16 [{x2d.shape[0]}, >= {world * n_local}] with unit inner "
+                        f"stride on {dev}")
+
+
 class _SharedBuffer:
     """One device buffer per rank, every rank's mapped into this process.
     Every step is collective: a rank whose set-up fails still takes part in
@@ -156,6 +185,7 @@ class PeerExchange:
             raise RuntimeError("PeerExchange is closed")
         if self._failed is not None:
             raise RuntimeError(f"PeerExchange failed: {self._failed}; close() it on every rank and set up a new one")
+        check_exchange_operands(x2d, weight_int8, scale, bias, out, self.world)
         M = x2d.shape[0]
         n_local = weight_int8.shape[0]
         if M > self.max_rows or n_local > self.max_n_local:
@@ -284,6 +314,7 @@ class PrefillExchange:
         if self._failed is not None:
             raise RuntimeError(f"PrefillExchange failed: {self._failed}; close() it on every rank and set up a "
                                "new one")
+        check_exchange_operands(x2d, weight_int8, scale, bias, out, self.world)
         M, K = x2d.shape
         n_local = weight_int8.shape[0]
         if not self.supports(M, n_local):

@@ -231,3 +231,18 @@ def test_prefill_exchange_needs_a_process_group():
         pytest.skip("a process group is already initialised")
     with pytest.raises(RuntimeError, match="process group"):
         PrefillExchange()
+
+
+def test_exchange_operand_checks():
+    """The exchanges pass raw pointers on: wrong dtypes, devices, shapes or
+    strides are refused on the host before anything reaches the library."""
+    from rotalabs_accel_b200.peer import check_exchange_operands
+    x = torch.zeros(4, 64, dtype=torch.float16)
+    w = torch.zeros(32, 64, dtype=torch.int8)
+    s = torch.ones(32)
+    with pytest.raises(TypeError, match="CUDA"):
+        check_exchange_operands(x, w, s, None, None, 2)           # CPU tensors never reach the kernels
+    with pytest.raises(TypeError, match="float16"):
+        check_exchange_operands(x.to(torch.bfloat16), w, s, None, None, 2)
+    with pytest.raises(TypeError, match="float16"):
+        check_exchange_operands(x[:, ::2], w, s, None, None, 2)   # strided rows
